@@ -1,0 +1,413 @@
+#!/usr/bin/env python
+"""ViT forward-pass throughput on B200, one process per GPU (BASELINE config 4 by default:
+ViT-B/16, BF16, batch 256 per GPU, logits gathered to rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--config vit-b|vit-s|vit-ti|vit-l]
+
+Under torchrun (N > 1) every rank runs its own replica on its own batch shard; the only
+collective is the per-step gather of the logits to rank 0 (NCCL). A step is one forward
+pass over one batch. Rank 0 prints one JSON line.
+
+  value   images/s over all ranks, inputs resident in HBM, CUDA-graph replay, timed with CUDA
+          events on the launching stream, max over ranks
+  e2e     the same through the public host-buffer call (VisionTransformer.forward_host: pinned
+          host images -> device, forward, logits -> host, synchronise) every step
+  roofline  the tcgen05 GEMMs (the dominant kernel): algorithmic FLOPs / device time of every
+          GEMM launch, from CUDA events around each launch over profiled passes
+  cpu_baseline  the reference's own CPU forward pass (oracle/_ref, compiled from its sources)
+          on this host's cores, one image per core, rank 0 at N = 1
+
+--impl reference times that CPU implementation alone (rank 0; other ranks exit).
+"""
+
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import pathlib
+import statistics
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+
+ROOT = pathlib.Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+sys.path.insert(0, str(ROOT / "cu-vit_b200"))
+
+import numpy as np  # noqa: E402
+
+METRIC = "ViT-B/16 images/s at 1/2/4/8 B200; batched-GEMM % of tensor-core peak"
+
+CONFIGS = {
+    # name: (model label, VitConfig kwargs, batch per GPU, precision, seed)
+    "vit-b": ("ViT-B/16", dict(embed_dim=768, heads=12, mlp_hidden=3072), 256, "bf16", 3),
+    "vit-s": ("ViT-S/16", dict(embed_dim=384, heads=6, mlp_hidden=1536), 128, "bf16", 2),
+    "vit-ti": ("ViT-Ti/16", dict(), 32, "tf32", 1),
+    "vit-l": ("ViT-L/16", dict(embed_dim=1024, depth=24, heads=16, mlp_hidden=4096), 128,
+              "bf16", 4),
+}
+
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def parse_args():
+    parser = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    parser.add_argument("--gpus", type=int, default=1)
+    parser.add_argument("--steps", type=int, default=50)
+    parser.add_argument("--warmup", type=int, default=5)
+    parser.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    parser.add_argument("--config", choices=sorted(CONFIGS), default="vit-b")
+    parser.add_argument("--profile-passes", type=int, default=3)
+    parser.add_argument("--no-cpu-baseline", action="store_true")
+    return parser.parse_args()
+
+
+def peaks() -> tuple[dict, str]:
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        return json.loads(path.read_text()), "measured"
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi samples of SM clock and throttle reasons, every 100 ms, with timestamps."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu_index = gpu_index
+        self.samples: list[tuple[float, list[str]]] = []
+        self._process = None
+        self._thread = None
+
+    def start(self) -> None:
+        try:
+            self._process = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100", "-i", str(self.gpu_index)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self._process = None
+            return
+        self._thread = threading.Thread(target=self._read, daemon=True)
+        self._thread.start()
+
+    def _read(self) -> None:
+        for line in self._process.stdout:
+            self.samples.append((time.monotonic(), [f.strip() for f in line.split(",")]))
+
+    def stop(self) -> None:
+        if self._process is not None:
+            self._process.terminate()
+            try:
+                self._process.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self._process.kill()
+        if self._thread is not None:
+            self._thread.join(timeout=5)
+
+    def summary(self, start: float, end: float) -> dict:
+        window = [s for t, s in self.samples if start <= t <= end]
+        if len(window) < 3:  # short timed region: widen into the warm-up, same load
+            window = [s for t, s in self.samples if start - 2.0 <= t <= end]
+        if not window:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({name for s in window for name, value in zip(names, s[5:9])
+                          if value.lower().startswith("active")})
+
+        def number(text):
+            try:
+                return float(text)
+            except ValueError:
+                return None
+
+        sm = [number(s[1]) for s in window if number(s[1]) is not None]
+        power = [number(s[3]) for s in window if number(s[3]) is not None]
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": number(window[0][2]), "reasons": reasons,
+                "power_w_median": statistics.median(power) if power else None,
+                "samples": len(window)}
+
+
+def write_cvw(config, weights, path) -> None:
+    from cuvit import cvw
+    from cuvit.vit import tensor_specs
+
+    writer = cvw.WeightFileWriter()
+    for name, extents in tensor_specs(config):
+        writer.add(name, extents, weights[name])
+    writer.write(path)
+
+
+def cpu_reference_step(config, weights_path, images, threads):
+    """One bounded sample of the workload through the reference's CPU code: returns
+    (seconds, images, kind)."""
+    import oracle
+
+    start = time.perf_counter()
+    if oracle.ref_cpu_available():
+        oracle.ref_vit_forward(weights_path, config, images, threads=threads)
+        kind = "reference"
+    else:
+        raise RuntimeError("oracle/_ref/libcuvit_ref_cpu.so is not built")
+    return time.perf_counter() - start, images.size // config.image_elements(), kind
+
+
+def reference_arm(args) -> None:
+    """Times the reference's own CPU implementation (oracle/_ref) on this host's cores."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from cuvit.vit import VitConfig, random_weights
+
+    label, kwargs, batch, precision, seed = CONFIGS[args.config]
+    config = VitConfig(**kwargs)
+    threads = os.cpu_count() or 1
+    weights = random_weights(config, seed)
+    rng = np.random.default_rng([seed, 0])
+    images = rng.standard_normal(threads * config.image_elements()).astype(np.float32)
+    with tempfile.TemporaryDirectory() as tmp:
+        path = pathlib.Path(tmp) / "weights.cvw"
+        write_cvw(config, weights, path)
+        for _ in range(args.warmup):
+            cpu_reference_step(config, path, images, threads)
+        total = 0.0
+        count = 0
+        for _ in range(args.steps):
+            seconds, n, kind = cpu_reference_step(config, path, images, threads)
+            total += seconds
+            count += n
+    value = count / total
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "images/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1000.0 * total / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic N(0,1) images, random-init trunc-normal(0.02) weights",
+        "config": {"workload": f"{label} forward, reference CPU implementation (FP32)",
+                   "model": label, "seq_len": config.token_count()},
+        "cpu_baseline": {"value": value, "unit": "images/s", "cores": threads, "kind": kind,
+                         "sample": f"{threads} images per step, one per host thread, "
+                                   "VitReference::forward (tests/reference/vit.hpp)"},
+        "e2e": {"value": value, "unit": "images/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def our_arm(args) -> None:
+    import torch
+    import torch.distributed as dist
+
+    import cuvit
+    from cuvit.vit import (PRECISION_BF16, PRECISION_TF32, VisionTransformer, VitConfig,
+                           random_weights)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
+                                device_id=device)
+
+    label, kwargs, batch, precision_name, seed = CONFIGS[args.config]
+    config = VitConfig(**kwargs)
+    precision = PRECISION_BF16 if precision_name == "bf16" else PRECISION_TF32
+    weights = random_weights(config, seed)
+    model = VisionTransformer(config, weights, max_batch=batch, precision=precision,
+                              device=local_rank)
+    rng = np.random.default_rng([seed, rank])
+    host_images = rng.standard_normal(batch * config.image_elements()).astype(np.float32)
+    images = torch.from_numpy(host_images).to(device)
+    logits = torch.zeros(batch, config.classes, device=device)
+    gathered = ([torch.zeros_like(logits) for _ in range(world)]
+                if (world > 1 and rank == 0) else None)
+    stream = torch.cuda.current_stream(device)
+
+    def step():
+        model.forward_graph(images, logits, batch, stream)
+        if world > 1:
+            dist.gather(logits, gathered, dst=0)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+        torch.cuda.synchronize(device)
+
+    def max_over_ranks(value: float) -> float:
+        if world == 1:
+            return value
+        t = torch.tensor([value], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    sampler = ClockSampler(local_rank)
+    sampler.start()
+    for _ in range(args.warmup):
+        step()
+    barrier()
+    launches_before = cuvit.kernels.launch_count()
+    start_event = torch.cuda.Event(enable_timing=True)
+    end_event = torch.cuda.Event(enable_timing=True)
+    t0 = time.monotonic()
+    start_event.record(stream)
+    for _ in range(args.steps):
+        step()
+    end_event.record(stream)
+    barrier()
+    t1 = time.monotonic()
+    elapsed_ms = max_over_ranks(start_event.elapsed_time(end_event))
+    clocks = sampler.summary(t0, t1)
+    sampler.stop()
+    gpu_launches = model.launches_per_forward(batch) * args.steps
+    launches_issued = cuvit.kernels.launch_count() - launches_before  # 0 under graph replay
+
+    # Per-kernel device time over a few profiled passes (events around each launch).
+    records = []
+    for _ in range(args.profile_passes):
+        records += model.forward_profiled(images, logits, batch, stream)
+    by_kind: dict[str, dict] = {}
+    for r in records:
+        entry = by_kind.setdefault(r["kind"], {"launches": 0, "ms": 0.0, "flops": 0.0,
+                                               "bytes": 0.0})
+        entry["launches"] += 1
+        entry["ms"] += r["ms"]
+        entry["flops"] += r["flops"]
+        entry["bytes"] += r["bytes"]
+    passes = max(args.profile_passes, 1)
+    profiled_ms = sum(e["ms"] for e in by_kind.values()) / passes
+    kernels = {}
+    for kind, e in sorted(by_kind.items()):
+        kernels[kind] = {
+            "launches_per_pass": e["launches"] // passes,
+            "ms_per_pass": e["ms"] / passes,
+            "share": e["ms"] / passes / profiled_ms if profiled_ms else None,
+            "tflops": e["flops"] / (e["ms"] * 1e-3) / 1e12 if e["flops"] else None,
+            "gbs": e["bytes"] / (e["ms"] * 1e-3) / 1e9,
+        }
+    gemm = [e for k, e in by_kind.items() if k.startswith("gemm")]
+    gemm_flops = sum(e["flops"] for e in gemm)
+    gemm_ms = sum(e["ms"] for e in gemm)
+    gemm_launches = sum(e["launches"] for e in gemm)
+    achieved_tflops = gemm_flops / (gemm_ms * 1e-3) / 1e12
+    peak, peak_kind = peaks()
+    traffic = None
+    traffic_file = ROOT / "profiles" / "traffic.json"
+    if traffic_file.exists():
+        traffic = json.loads(traffic_file.read_text()).get(f"{args.config}/gemm")
+
+    # End to end through the public host-buffer API: pinned host images in, logits out.
+    pinned_images = torch.from_numpy(host_images).pin_memory()
+    pinned_logits = torch.zeros(batch, config.classes).pin_memory()
+    device_logits = torch.zeros_like(logits)
+
+    def e2e_step():
+        model.forward_host_ptr(pinned_images.data_ptr(), pinned_logits.data_ptr(), batch,
+                               stream)
+        if world > 1:
+            device_logits.copy_(pinned_logits, non_blocking=False)
+            dist.gather(device_logits, gathered, dst=0)
+
+    for _ in range(args.warmup):
+        e2e_step()
+    barrier()
+    e2e_start = torch.cuda.Event(enable_timing=True)
+    e2e_end = torch.cuda.Event(enable_timing=True)
+    e2e_start.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    e2e_end.record(stream)
+    barrier()
+    e2e_ms = max_over_ranks(e2e_start.elapsed_time(e2e_end))
+
+    cpu_baseline = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu_baseline = measure_cpu_baseline(config, weights, seed)
+
+    total_images = world * batch * args.steps
+    value = total_images / (elapsed_ms * 1e-3)
+    if rank == 0:
+        bf16 = precision == PRECISION_BF16
+        sustained = peak.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"])
+        burst = peak.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"])
+        line = {
+            "metric": METRIC, "value": value, "unit": "images/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": elapsed_ms / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16" if bf16 else "tf32",
+            "data": "synthetic N(0,1) images, random-init trunc-normal(0.02) weights",
+            "config": {
+                "workload": f"{label} forward, {precision_name.upper()} operands / FP32 "
+                            f"accumulate, batch {batch} per GPU",
+                "model": label, "global_batch": batch * world, "seq_len": config.token_count(),
+                "parallelism": f"dp{world} (replicas; logits gathered to rank 0 each step)",
+                "l2": f"inputs {host_images.nbytes / 1e6:.0f} MB per GPU (> 126 MB L2), "
+                      "weights re-read each pass; no flush",
+                "gflop_per_image": config.gflop_per_image(),
+            },
+            "e2e": {"value": total_images / (e2e_ms * 1e-3), "unit": "images/s",
+                    "h2d_bytes_per_step": int(host_images.nbytes),
+                    "d2h_bytes_per_step": int(batch * config.classes * 4)},
+            "gpu_launches": gpu_launches,
+            "roofline": {
+                "kernel": "tc_gemm_kernel (all GEMM launches of a pass)",
+                "bound": "tensor", "achieved": achieved_tflops,
+                "peak": sustained, "unit": "TFLOP/s", "frac": achieved_tflops / sustained,
+                "peak_kind": f"{peak_kind} bf16 sustained (GEMMs run inside a long step)",
+                "frac_of_burst": achieved_tflops / burst,
+                "frac_of_nominal_2250": achieved_tflops / 2250.0,
+                "traffic": traffic,
+                "launches_per_pass": gemm_launches // passes,
+                "flops_per_launch": gemm_flops / max(gemm_launches, 1),
+            },
+            "kernels": kernels,
+            "clocks": clocks,
+            "cpu_baseline": cpu_baseline,
+            "launches_issued_in_timed_region": launches_issued,
+        }
+        print(json.dumps(line), flush=True)
+    model.close()
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def measure_cpu_baseline(config, weights, seed) -> dict | None:
+    """The reference's CPU forward on one image per host core (about 10-30 s)."""
+    import oracle
+
+    threads = os.cpu_count() or 1
+    rng = np.random.default_rng([seed, 99])
+    images = rng.standard_normal(threads * config.image_elements()).astype(np.float32)
+    try:
+        with tempfile.TemporaryDirectory() as tmp:
+            path = pathlib.Path(tmp) / "weights.cvw"
+            write_cvw(config, weights, path)
+            seconds, count, kind = cpu_reference_step(config, path, images, threads)
+    except (RuntimeError, FileNotFoundError) as error:
+        return {"value": None, "unit": "images/s", "cores": threads, "kind": None,
+                "sample": f"unavailable: {error}"}
+    return {"value": count / seconds, "unit": "images/s", "cores": threads, "kind": kind,
+            "sample": f"{count} images, one per host thread, VitReference::forward "
+                      f"(tests/reference/vit.hpp), {seconds:.1f} s"}
+
+
+def main() -> None:
+    args = parse_args()
+    if args.impl == "reference":
+        reference_arm(args)
+    else:
+        our_arm(args)
+
+
+if __name__ == "__main__":
+    main()

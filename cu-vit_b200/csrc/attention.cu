@@ -1,0 +1,395 @@
+// Fused multi-head attention for ViT token counts (T <= 256, head_dim 64).
+//
+// Replaces the reference's three launches per block -- Q.K^T into a [B, h, T, T] logits
+// buffer, an in-place row softmax, and P.V (src/model/vit.cu:205-242) -- with one kernel per
+// (image, head) that never writes the logits to HBM:
+//
+//   1. TMA brings Q (two 128-row tiles), K and V of one head into shared memory with
+//      128-byte swizzle, straight out of the packed [T, 3, h, d] projection rows.
+//   2. One thread issues S = Q.K^T (tcgen05, K-major operands) into tensor memory.
+//   3. Four softmax warps, one thread per query row, read their S row from TMEM twice (row
+//      max, then exp/sum), and write P back into the same TMEM columns: packed bf16 pairs
+//      for BF16, FP32 values (read as TF32) for the FP32 path.
+//   4. O = P.V is issued with A = P read from TMEM and B = V (MN-major) from shared memory.
+//   5. The softmax warps scale O by 1/rowsum and store it into the [T, h*d] context layout
+//      the output projection reads.
+//
+// All T keys fit one tile, so the softmax is exact (no online rescaling).
+#include "cuvit_b200.h"
+#include "ptx.cuh"
+#include "runtime.hpp"
+
+#include <cuda_bf16.h>
+
+#include <cstdint>
+#include <mutex>
+
+namespace cuvit::attn {
+namespace {
+
+constexpr int kHeadDim = 64;
+constexpr int kTileQ = 128;
+constexpr int kMaxTokens = 256;
+constexpr int kThreads = 192; // warp 0 issuer, warp 1 TMEM, warps 2..5 softmax
+
+struct Params {
+    int tokens;
+    int heads;
+    int n_keys;  // tokens rounded up to 16 (MMA N)
+    int q_tiles; // ceil(tokens / 128)
+    float scale_log2; // scale * log2(e)
+    float scale;
+    void* context;
+    unsigned* status;
+};
+
+template <int ElemBytes>
+struct Layout {
+    static constexpr int kAtomElems = 128 / ElemBytes;           // elements per 128-byte row
+    static constexpr int kDAtoms = kHeadDim / kAtomElems;        // 1 (bf16) or 2 (fp32)
+    static constexpr int kMmaK = 32 / ElemBytes;                 // K per MMA instruction
+    static constexpr int kQTileBytes = kDAtoms * kTileQ * 128;   // one 128-row Q tile
+    static constexpr uint32_t kTmemColumns = ElemBytes == 2 ? 256 : 512;
+    static constexpr int kOColumn = ElemBytes == 2 ? 128 : 256;
+    // Minimum dynamic shared memory, chosen so TMEM demand per SM stays within 512 columns.
+    static constexpr int kMinSmem = ElemBytes == 2 ? 80 * 1024 : 120 * 1024;
+};
+
+template <int ElemBytes>
+__global__ void __launch_bounds__(kThreads)
+    attention_kernel(const __grid_constant__ CUtensorMap map_q,
+                     const __grid_constant__ CUtensorMap map_kv, const Params p) {
+    using L = Layout<ElemBytes>;
+    using T = typename std::conditional<ElemBytes == 2, __nv_bfloat16, float>::type;
+    constexpr dev::MmaKind kKind = ElemBytes == 2 ? dev::MmaKind::kF16 : dev::MmaKind::kTF32;
+    constexpr uint32_t kFormat = ElemBytes == 2 ? 1u : 2u;
+
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw_base = dev::smem_u32(smem_raw);
+    const uint32_t base = (raw_base + 1023u) & ~1023u;
+    uint8_t* const smem = smem_raw + (base - raw_base);
+
+    const int kv_region = p.n_keys * 128; // one 128-byte-wide column block of K or V
+    const uint32_t q_smem = base;
+    const uint32_t k_smem = q_smem + p.q_tiles * L::kQTileBytes;
+    const uint32_t v_smem = k_smem + L::kDAtoms * kv_region;
+    const uint32_t bar_base = v_smem + L::kDAtoms * kv_region;
+    const uint32_t bar_load = bar_base;
+    const uint32_t bar_s = bar_base + 8;
+    const uint32_t bar_p = bar_base + 16;
+    const uint32_t bar_o = bar_base + 24;
+    const uint32_t bar_free = bar_base + 32;
+    const uint32_t bar_drain = bar_base + 40;
+    uint32_t* const tmem_slot = reinterpret_cast<uint32_t*>(smem + (bar_base - base) + 48);
+
+    const int warp = threadIdx.x / 32;
+    const int lane = threadIdx.x % 32;
+    const int image = blockIdx.x / p.heads;
+    const int head = blockIdx.x - image * p.heads;
+
+    if (threadIdx.x == 0) {
+        dev::mbar_init(bar_load, 1);
+        dev::mbar_init(bar_s, 1);
+        dev::mbar_init(bar_p, 128);
+        dev::mbar_init(bar_o, 1);
+        dev::mbar_init(bar_free, 128);
+        dev::mbar_init(bar_drain, 1);
+        dev::fence_barrier_init();
+    }
+    if (warp == 1) {
+        dev::tmem_alloc(dev::smem_u32(tmem_slot), L::kTmemColumns);
+        dev::tmem_relinquish();
+    }
+    dev::tc_fence_before();
+    __syncthreads();
+    dev::tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0 && lane == 0) {
+        // ---------------- loads and MMA issue ----------------
+        dev::tma_prefetch_descriptor(&map_q);
+        dev::tma_prefetch_descriptor(&map_kv);
+        const int hd = p.heads * kHeadDim;
+        const uint32_t bytes = static_cast<uint32_t>(p.q_tiles * L::kQTileBytes +
+                                                     2 * L::kDAtoms * kv_region);
+        dev::mbar_arrive_expect_tx(bar_load, bytes);
+        for (int t = 0; t < p.q_tiles; ++t) {
+            for (int j = 0; j < L::kDAtoms; ++j) {
+                const int c[3] = {head * kHeadDim + j * L::kAtomElems, t * kTileQ, image};
+                dev::tma_load(q_smem + t * L::kQTileBytes + j * kTileQ * 128, &map_q, bar_load, 3,
+                              c);
+            }
+        }
+        for (int j = 0; j < L::kDAtoms; ++j) {
+            const int ck[3] = {hd + head * kHeadDim + j * L::kAtomElems, 0, image};
+            dev::tma_load(k_smem + j * kv_region, &map_kv, bar_load, 3, ck);
+            const int cv[3] = {2 * hd + head * kHeadDim + j * L::kAtomElems, 0, image};
+            dev::tma_load(v_smem + j * kv_region, &map_kv, bar_load, 3, cv);
+        }
+        bool ok = dev::mbar_wait(bar_load, 0, p.status);
+        const uint32_t idesc_s = dev::make_idesc(kFormat, kTileQ, p.n_keys, false, false);
+        constexpr uint32_t kIdescO = dev::make_idesc(kFormat, kTileQ, kHeadDim, false, true);
+        constexpr int kStepsPerAtom = L::kAtomElems / L::kMmaK;
+        for (int t = 0; t < p.q_tiles && ok; ++t) {
+            if (t > 0 && !dev::mbar_wait(bar_free, (t - 1) & 1, p.status)) {
+                ok = false;
+                break;
+            }
+            dev::tc_fence_after();
+            // S = Q_t . K^T
+#pragma unroll
+            for (int kk = 0; kk < kHeadDim / L::kMmaK; ++kk) {
+                const int atom = kk / kStepsPerAtom;
+                const uint32_t offset = (kk % kStepsPerAtom) * 32;
+                const uint64_t a_desc = dev::smem_desc_sw128(
+                    q_smem + t * L::kQTileBytes + atom * kTileQ * 128 + offset, 16, 1024);
+                const uint64_t b_desc =
+                    dev::smem_desc_sw128(k_smem + atom * kv_region + offset, 16, 1024);
+                dev::mma_ss<kKind>(tmem, a_desc, b_desc, idesc_s, kk > 0 ? 1u : 0u);
+            }
+            dev::tc_commit(bar_s);
+            if (!dev::mbar_wait(bar_p, t & 1, p.status)) {
+                ok = false;
+                break;
+            }
+            dev::tc_fence_after();
+            // O = P . V, P read from TMEM columns [0, n_keys * ElemBytes / 4)
+            const int steps = p.n_keys / L::kMmaK;
+            for (int kk = 0; kk < steps; ++kk) {
+                const uint32_t a_tmem = tmem + static_cast<uint32_t>(kk * 8);
+                const uint64_t b_desc = dev::smem_desc_sw128(
+                    v_smem + kk * L::kMmaK * 128, static_cast<uint32_t>(kv_region), 1024);
+                dev::mma_ts<kKind>(tmem + L::kOColumn, a_tmem, b_desc, kIdescO,
+                                   kk > 0 ? 1u : 0u);
+            }
+            dev::tc_commit(bar_o);
+        }
+        if (!ok) {
+            // Wait until every MMA issued so far has finished before the CTA tears down.
+            dev::tc_commit(bar_drain);
+            dev::mbar_wait(bar_drain, 0, p.status);
+        }
+    } else if (warp >= 2) {
+        // ---------------- softmax and output ----------------
+        const int quarter = warp & 3;
+        const int row = quarter * 32 + lane;
+        const uint32_t lane_field = static_cast<uint32_t>(quarter * 32) << 16;
+        const int chunks = (p.n_keys + 31) / 32;
+        for (int t = 0; t < p.q_tiles; ++t) {
+            if (!dev::mbar_wait(bar_s, t & 1, p.status)) {
+                break;
+            }
+            dev::tc_fence_after();
+            float maximum = -INFINITY;
+            for (int c = 0; c < chunks; ++c) {
+                uint32_t s[32];
+                dev::tmem_load_32(tmem + lane_field + c * 32, s);
+                dev::tmem_wait_load();
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    if (c * 32 + j < p.tokens) {
+                        maximum = fmaxf(maximum, __uint_as_float(s[j]) * p.scale);
+                    }
+                }
+            }
+            const float offset = maximum * 1.4426950408889634F;
+            float sum = 0.0F;
+            for (int c = 0; c < chunks; ++c) {
+                uint32_t s[32];
+                dev::tmem_load_32(tmem + lane_field + c * 32, s);
+                dev::tmem_wait_load();
+                float e[32];
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    e[j] = c * 32 + j < p.tokens
+                               ? exp2f(__uint_as_float(s[j]) * p.scale_log2 - offset)
+                               : 0.0F;
+                }
+                if constexpr (ElemBytes == 2) {
+                    uint32_t packed[16];
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        packed[j] = dev::pack_bf16x2(e[2 * j], e[2 * j + 1]);
+                        const __nv_bfloat162 pair =
+                            *reinterpret_cast<const __nv_bfloat162*>(&packed[j]);
+                        const float2 rounded = __bfloat1622float2(pair);
+                        sum += rounded.x + rounded.y;
+                    }
+                    dev::tmem_store_16(tmem + lane_field + c * 16, packed);
+                } else {
+                    uint32_t lo[16];
+                    uint32_t hi[16];
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        lo[j] = __float_as_uint(e[j]);
+                        hi[j] = __float_as_uint(e[16 + j]);
+                        sum += e[j] + e[16 + j];
+                    }
+                    dev::tmem_store_16(tmem + lane_field + c * 32, lo);
+                    dev::tmem_store_16(tmem + lane_field + c * 32 + 16, hi);
+                }
+            }
+            dev::tmem_wait_store();
+            dev::tc_fence_before();
+            dev::mbar_arrive(bar_p);
+            if (!dev::mbar_wait(bar_o, t & 1, p.status)) {
+                break;
+            }
+            dev::tc_fence_after();
+            uint32_t o0[32];
+            uint32_t o1[32];
+            dev::tmem_load_32(tmem + lane_field + L::kOColumn, o0);
+            dev::tmem_load_32(tmem + lane_field + L::kOColumn + 32, o1);
+            dev::tmem_wait_load();
+            const float inverse = 1.0F / sum;
+            const int query = t * kTileQ + row;
+            if (query < p.tokens) {
+                T* const out = static_cast<T*>(p.context) +
+                               (static_cast<long long>(image) * p.tokens + query) * p.heads *
+                                   kHeadDim +
+                               head * kHeadDim;
+                if constexpr (ElemBytes == 2) {
+                    uint4* const out4 = reinterpret_cast<uint4*>(out);
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        out4[q] = make_uint4(
+                            dev::pack_bf16x2(__uint_as_float(o0[8 * q]) * inverse,
+                                             __uint_as_float(o0[8 * q + 1]) * inverse),
+                            dev::pack_bf16x2(__uint_as_float(o0[8 * q + 2]) * inverse,
+                                             __uint_as_float(o0[8 * q + 3]) * inverse),
+                            dev::pack_bf16x2(__uint_as_float(o0[8 * q + 4]) * inverse,
+                                             __uint_as_float(o0[8 * q + 5]) * inverse),
+                            dev::pack_bf16x2(__uint_as_float(o0[8 * q + 6]) * inverse,
+                                             __uint_as_float(o0[8 * q + 7]) * inverse));
+                        out4[4 + q] = make_uint4(
+                            dev::pack_bf16x2(__uint_as_float(o1[8 * q]) * inverse,
+                                             __uint_as_float(o1[8 * q + 1]) * inverse),
+                            dev::pack_bf16x2(__uint_as_float(o1[8 * q + 2]) * inverse,
+                                             __uint_as_float(o1[8 * q + 3]) * inverse),
+                            dev::pack_bf16x2(__uint_as_float(o1[8 * q + 4]) * inverse,
+                                             __uint_as_float(o1[8 * q + 5]) * inverse),
+                            dev::pack_bf16x2(__uint_as_float(o1[8 * q + 6]) * inverse,
+                                             __uint_as_float(o1[8 * q + 7]) * inverse));
+                    }
+                } else {
+                    float4* const out4 = reinterpret_cast<float4*>(out);
+#pragma unroll
+                    for (int q = 0; q < 8; ++q) {
+                        out4[q] = make_float4(__uint_as_float(o0[4 * q]) * inverse,
+                                              __uint_as_float(o0[4 * q + 1]) * inverse,
+                                              __uint_as_float(o0[4 * q + 2]) * inverse,
+                                              __uint_as_float(o0[4 * q + 3]) * inverse);
+                        out4[8 + q] = make_float4(__uint_as_float(o1[4 * q]) * inverse,
+                                                  __uint_as_float(o1[4 * q + 1]) * inverse,
+                                                  __uint_as_float(o1[4 * q + 2]) * inverse,
+                                                  __uint_as_float(o1[4 * q + 3]) * inverse);
+                    }
+                }
+            }
+            dev::tc_fence_before();
+            dev::mbar_arrive(bar_free);
+        }
+    }
+
+    __syncthreads();
+    if (warp == 1) {
+        dev::tc_fence_after();
+        dev::tmem_dealloc(tmem, L::kTmemColumns);
+    }
+}
+
+template <int ElemBytes>
+int launch_typed(const void* qkv, void* context, int batch, int tokens, int heads, float scale,
+                 const host::DeviceContext& device, cudaStream_t stream) {
+    using L = Layout<ElemBytes>;
+    const int n_keys = (tokens + 15) / 16 * 16;
+    const int q_tiles = (tokens + kTileQ - 1) / kTileQ;
+    const int row = 3 * heads * kHeadDim;
+
+    host::TmaTensor tq;
+    tq.base = qkv;
+    tq.type = ElemBytes == 2 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+    tq.element_bytes = ElemBytes;
+    tq.rank = 3;
+    tq.dims[0] = static_cast<uint64_t>(row);
+    tq.dims[1] = static_cast<uint64_t>(tokens);
+    tq.dims[2] = static_cast<uint64_t>(batch);
+    tq.strides_bytes[0] = static_cast<uint64_t>(row) * ElemBytes;
+    tq.strides_bytes[1] = static_cast<uint64_t>(row) * tokens * ElemBytes;
+    tq.box[0] = L::kAtomElems;
+    tq.box[1] = kTileQ;
+    tq.box[2] = 1;
+    host::TmaTensor tkv = tq;
+    tkv.box[1] = static_cast<uint32_t>(n_keys);
+
+    CUtensorMap map_q;
+    CUtensorMap map_kv;
+    CUVIT_TRY(host::encode_tma(tq, &map_q));
+    CUVIT_TRY(host::encode_tma(tkv, &map_kv));
+
+    Params params;
+    params.tokens = tokens;
+    params.heads = heads;
+    params.n_keys = n_keys;
+    params.q_tiles = q_tiles;
+    params.scale = scale;
+    params.scale_log2 = scale * 1.4426950408889634F;
+    params.context = context;
+    params.status = device.status;
+
+    int smem = 1024 + q_tiles * L::kQTileBytes + 2 * L::kDAtoms * n_keys * 128 + 64;
+    if (smem < L::kMinSmem) {
+        smem = L::kMinSmem;
+    }
+    auto* kernel = &attention_kernel<ElemBytes>;
+    static std::once_flag once;
+    static cudaError_t attribute_error = cudaSuccess;
+    std::call_once(once, [kernel]() {
+        attribute_error = cudaFuncSetAttribute(
+            kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    });
+    CUVIT_TRY_CUDA(attribute_error);
+    kernel<<<batch * heads, kThreads, smem, stream>>>(map_q, map_kv, params);
+    return host::after_launch("attention_kernel");
+}
+
+} // namespace
+} // namespace cuvit::attn
+
+extern "C" int cuvit_attention(const void* qkv, void* context, int dtype, int batch, int tokens,
+                               int heads, int head_dim, float scale, cuvit_stream_t stream) {
+    using cuvit::host::fail;
+    if (batch == 0) {
+        return CUVIT_OK;
+    }
+    if (batch < 0 || tokens <= 0 || heads <= 0 || head_dim <= 0) {
+        return fail(CUVIT_INVALID_ARGUMENT, "attention extents must be positive");
+    }
+    if (qkv == nullptr || context == nullptr) {
+        return fail(CUVIT_INVALID_ARGUMENT, "attention operands cannot be null");
+    }
+    if (dtype != CUVIT_DTYPE_BF16 && dtype != CUVIT_DTYPE_F32) {
+        return fail(CUVIT_INVALID_ARGUMENT, "attention data type must be BF16 or F32");
+    }
+    if (head_dim != cuvit::attn::kHeadDim || tokens > cuvit::attn::kMaxTokens) {
+        return fail(CUVIT_UNSUPPORTED,
+                    "fused attention supports head_dim 64 and at most 256 tokens");
+    }
+    if (reinterpret_cast<uintptr_t>(qkv) % 16 != 0 ||
+        reinterpret_cast<uintptr_t>(context) % 16 != 0) {
+        return fail(CUVIT_INVALID_ARGUMENT, "attention operands must be 16-byte aligned");
+    }
+    if (static_cast<long long>(batch) * heads > 0x7FFFFFFFLL) {
+        return fail(CUVIT_LENGTH_ERROR, "attention launch exceeds the CUDA grid limit");
+    }
+    const cuvit::host::DeviceContext* device = nullptr;
+    CUVIT_TRY(cuvit::host::current_context(&device));
+    if (!cuvit::host::is_blackwell(*device)) {
+        return fail(CUVIT_UNSUPPORTED, "fused attention needs an sm_100 device");
+    }
+    const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    if (dtype == CUVIT_DTYPE_BF16) {
+        return cuvit::attn::launch_typed<2>(qkv, context, batch, tokens, heads, scale, *device, s);
+    }
+    return cuvit::attn::launch_typed<4>(qkv, context, batch, tokens, heads, scale, *device, s);
+}

@@ -1,0 +1,452 @@
+// Persistent, warp-specialised tcgen05 GEMM for sm_100a.
+//
+//   C[e][m][n] = epilogue(alpha * sum_k A[e][m][k] * B[e](k, n) + bias[n])
+//
+// A is row-major [M, K] (K-major). B is either [N, K] (K-major, the reference's
+// kTransposed layout) or [K, N] (MN-major, kNoTranspose). Operands arrive by TMA with
+// 128-byte swizzle into a ring of shared-memory stages; one thread issues tcgen05.mma into
+// a double-buffered FP32 accumulator in tensor memory; four epilogue warps drain TMEM,
+// apply alpha / bias / GELU / accumulate and store C while the next tile accumulates.
+//
+// Roles (one CTA per SM, persistent over output tiles 128 x BN):
+//   warp 0        TMA producer (one elected lane)
+//   warp 1        MMA issuer (one elected lane)
+//   warp 2        TMEM allocator
+//   warps 4..7    epilogue, warp w owns TMEM lanes 32*(w%4) .. +31 (= tile rows)
+//   warps 8..11   (Split only) 3xTF32 splitter: rewrites each landed stage as
+//                 hi = tf32(x) in place and lo = x - hi beside it, so the MMA warp can
+//                 issue hi*hi + hi*lo + lo*hi.
+//
+// Numerics: each output element's K reduction runs in a fixed order that depends only on
+// K (no split-K), so results do not depend on M, the batch, or the tile chosen for M.
+#pragma once
+
+#include "ptx.cuh"
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+
+#include <cstdint>
+
+namespace cuvit::gemm {
+
+constexpr int kBlockM = 128;
+constexpr int kSwizzleBytes = 128; // one swizzle atom row
+constexpr int kSmemBudget = 196608; // operand stages per CTA
+
+struct TcParams {
+    int m, n, k;
+    int m_tiles, n_tiles, k_blocks;
+    int total_tiles;
+    int count, inner; // batch entries; inner > 0 splits entry e into (e / inner, e % inner)
+    int a_rank, b_rank;
+    int a_has_index, a_has_outer, b_has_index, b_has_outer;
+    float alpha;
+    const float* bias;
+    void* c;
+    long long ldc, stride_c, outer_stride_c;
+    int c_bf16;
+    int c_vector_ok; // 16-byte vector stores of whole 32-column chunks are aligned
+    int accumulate, gelu;
+    unsigned* status;
+};
+
+template <int ElemBytes, int BN, bool Split>
+struct TcShape {
+    static constexpr int kBlockK = kSwizzleBytes / ElemBytes;       // K elements per stage
+    static constexpr int kMmaK = 32 / ElemBytes;                     // K per instruction
+    static constexpr int kAtomElems = kSwizzleBytes / ElemBytes;     // MN elements per atom
+    static constexpr int kABytes = kBlockM * kSwizzleBytes;          // 16 KiB
+    static constexpr int kBBytes = BN * kSwizzleBytes;
+    static constexpr int kStageBytes = (kABytes + kBBytes) * (Split ? 2 : 1);
+    static constexpr int kStagesRaw = kSmemBudget / kStageBytes;
+    static constexpr int kStages = kStagesRaw > 8 ? 8 : kStagesRaw;
+    static constexpr int kTmemColumns = 2 * BN < 32 ? 32 : 2 * BN;
+    static constexpr int kThreads = Split ? 384 : 256;
+    // barriers: full, empty, converted (split) per stage; tmem full/empty x2; drain
+    static constexpr int kBarrierBytes = (3 * kStages + 5) * 8 + 16;
+    static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kBarrierBytes;
+    static_assert(kStages >= 2, "at least two pipeline stages");
+    static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "BN must be 32..256, multiple of 32");
+};
+
+__device__ __forceinline__ void batch_coords(int entry, int inner, int& index, int& outer) {
+    if (inner > 0) {
+        outer = entry / inner;
+        index = entry - outer * inner;
+    } else {
+        outer = 0;
+        index = entry;
+    }
+}
+
+// Rounds an FP32 value to the nearest TF32 (10-bit mantissa) value; non-finite values pass.
+__device__ __forceinline__ float round_to_tf32(float x) {
+    const uint32_t bits = __float_as_uint(x);
+    if ((bits & 0x7F800000u) == 0x7F800000u) {
+        return x;
+    }
+    const uint32_t rounded = (bits + 0x1000u) & 0xFFFFE000u;
+    // A carry into an all-ones exponent would turn a finite value into infinity.
+    if ((rounded & 0x7F800000u) == 0x7F800000u) {
+        return __uint_as_float(bits & 0xFFFFE000u);
+    }
+    return __uint_as_float(rounded);
+}
+
+template <int ElemBytes, int BN, bool BMnMajor, bool Split>
+__global__ void __launch_bounds__(TcShape<ElemBytes, BN, Split>::kThreads, 1)
+    tc_gemm_kernel(const __grid_constant__ CUtensorMap tma_a,
+                   const __grid_constant__ CUtensorMap tma_b, const TcParams p) {
+    using Shape = TcShape<ElemBytes, BN, Split>;
+    constexpr int kStages = Shape::kStages;
+    constexpr dev::MmaKind kKind = ElemBytes == 2 ? dev::MmaKind::kF16 : dev::MmaKind::kTF32;
+    constexpr uint32_t kFormat = ElemBytes == 2 ? 1u : 2u; // BF16 or TF32
+    constexpr uint32_t kIdesc = dev::make_idesc(kFormat, kBlockM, BN, false, BMnMajor);
+    constexpr uint32_t kTxBytes = Shape::kABytes + Shape::kBBytes;
+
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw_base = dev::smem_u32(smem_raw);
+    const uint32_t base = (raw_base + 1023u) & ~1023u;
+    uint8_t* const smem = smem_raw + (base - raw_base);
+
+    // Stage s: [A | B | A_lo | B_lo]
+    const auto stage_a = [&](int s) -> uint32_t { return base + s * Shape::kStageBytes; };
+    const auto stage_b = [&](int s) -> uint32_t {
+        return base + s * Shape::kStageBytes + Shape::kABytes;
+    };
+    const uint32_t bar_base = base + kStages * Shape::kStageBytes;
+    const auto full_bar = [&](int s) -> uint32_t { return bar_base + 8u * s; };
+    const auto empty_bar = [&](int s) -> uint32_t { return bar_base + 8u * (kStages + s); };
+    const auto conv_bar = [&](int s) -> uint32_t { return bar_base + 8u * (2 * kStages + s); };
+    const auto tfull_bar = [&](int a) -> uint32_t { return bar_base + 8u * (3 * kStages + a); };
+    const auto tempty_bar = [&](int a) -> uint32_t {
+        return bar_base + 8u * (3 * kStages + 2 + a);
+    };
+    const uint32_t drain_bar = bar_base + 8u * (3 * kStages + 4);
+    uint32_t* const tmem_slot =
+        reinterpret_cast<uint32_t*>(smem + (bar_base - base) + 8 * (3 * kStages + 5));
+
+    const int warp = threadIdx.x / 32;
+    const int lane = threadIdx.x % 32;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            dev::mbar_init(full_bar(s), 1);
+            dev::mbar_init(empty_bar(s), 1);
+            dev::mbar_init(conv_bar(s), 128);
+        }
+        for (int a = 0; a < 2; ++a) {
+            dev::mbar_init(tfull_bar(a), 1);
+            dev::mbar_init(tempty_bar(a), 128);
+        }
+        dev::mbar_init(drain_bar, 1);
+        dev::fence_barrier_init();
+    }
+    if (warp == 2) {
+        dev::tmem_alloc(dev::smem_u32(tmem_slot), Shape::kTmemColumns);
+        dev::tmem_relinquish();
+    }
+    dev::tc_fence_before();
+    __syncthreads();
+    dev::tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    const int per_entry = p.m_tiles * p.n_tiles;
+
+    if (warp == 0 && lane == 0) {
+        // ---------------- TMA producer ----------------
+        dev::tma_prefetch_descriptor(&tma_a);
+        dev::tma_prefetch_descriptor(&tma_b);
+        int stage = 0;
+        uint32_t phase = 0;
+        bool ok = true;
+        for (int tile = blockIdx.x; tile < p.total_tiles && ok; tile += gridDim.x) {
+            const int entry = tile / per_entry;
+            const int rest = tile - entry * per_entry;
+            const int m_block = rest / p.n_tiles;
+            const int n_block = rest - m_block * p.n_tiles;
+            int index, outer;
+            batch_coords(entry, p.inner, index, outer);
+            for (int kb = 0; kb < p.k_blocks; ++kb) {
+                if (!dev::mbar_wait(empty_bar(stage), phase ^ 1u, p.status)) {
+                    ok = false;
+                    break;
+                }
+                dev::mbar_arrive_expect_tx(full_bar(stage), kTxBytes);
+                const int k0 = kb * Shape::kBlockK;
+                int ca[4] = {k0, m_block * kBlockM, 0, 0};
+                int r = 2;
+                if (p.a_has_index) ca[r++] = index;
+                if (p.a_has_outer) ca[r++] = outer;
+                dev::tma_load(stage_a(stage), &tma_a, full_bar(stage), p.a_rank, ca);
+                if constexpr (!BMnMajor) {
+                    int cb[4] = {k0, n_block * BN, 0, 0};
+                    int rb = 2;
+                    if (p.b_has_index) cb[rb++] = index;
+                    if (p.b_has_outer) cb[rb++] = outer;
+                    dev::tma_load(stage_b(stage), &tma_b, full_bar(stage), p.b_rank, cb);
+                } else {
+                    // [K, N] operand: one box per 128-byte atom of N, each BK rows deep.
+#pragma unroll
+                    for (int atom = 0; atom < BN / Shape::kAtomElems; ++atom) {
+                        int cb[4] = {n_block * BN + atom * Shape::kAtomElems, k0, 0, 0};
+                        int rb = 2;
+                        if (p.b_has_index) cb[rb++] = index;
+                        if (p.b_has_outer) cb[rb++] = outer;
+                        dev::tma_load(stage_b(stage) + atom * Shape::kBlockK * kSwizzleBytes,
+                                      &tma_b, full_bar(stage), p.b_rank, cb);
+                    }
+                }
+                if (++stage == kStages) {
+                    stage = 0;
+                    phase ^= 1u;
+                }
+            }
+        }
+        if (!ok) {
+            // Let every load this thread issued land before the CTA can exit.
+            for (int s = 0; s < kStages; ++s) {
+                dev::mbar_wait(full_bar(s), phase ^ (s < stage ? 0u : 1u), p.status);
+            }
+        }
+    } else if (warp == 1 && lane == 0) {
+        // ---------------- MMA issuer ----------------
+        int stage = 0;
+        uint32_t phase = 0;
+        int local = 0;
+        bool ok = true;
+        for (int tile = blockIdx.x; tile < p.total_tiles && ok; tile += gridDim.x, ++local) {
+            const int acc = local & 1;
+            const uint32_t acc_phase = (local >> 1) & 1;
+            if (!dev::mbar_wait(tempty_bar(acc), acc_phase ^ 1u, p.status)) {
+                ok = false;
+                break;
+            }
+            dev::tc_fence_after();
+            const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+            for (int kb = 0; kb < p.k_blocks; ++kb) {
+                const uint32_t ready = Split ? conv_bar(stage) : full_bar(stage);
+                if (!dev::mbar_wait(ready, phase, p.status)) {
+                    ok = false;
+                    break;
+                }
+                dev::tc_fence_after();
+                const uint32_t a_addr = stage_a(stage);
+                const uint32_t b_addr = stage_b(stage);
+#pragma unroll
+                for (int kk = 0; kk < Shape::kBlockK / Shape::kMmaK; ++kk) {
+                    const uint64_t a_desc =
+                        dev::smem_desc_sw128(a_addr + kk * 32, 16, 1024);
+                    uint64_t b_desc;
+                    if constexpr (!BMnMajor) {
+                        b_desc = dev::smem_desc_sw128(b_addr + kk * 32, 16, 1024);
+                    } else {
+                        b_desc = dev::smem_desc_sw128(b_addr + kk * Shape::kMmaK * kSwizzleBytes,
+                                                      Shape::kBlockK * kSwizzleBytes, 1024);
+                    }
+                    const uint32_t accumulate = (kb > 0 || kk > 0) ? 1u : 0u;
+                    if constexpr (Split) {
+                        const uint32_t lo_offset = Shape::kABytes + Shape::kBBytes;
+                        uint64_t b_lo_desc;
+                        if constexpr (!BMnMajor) {
+                            b_lo_desc =
+                                dev::smem_desc_sw128(b_addr + lo_offset + kk * 32, 16, 1024);
+                        } else {
+                            b_lo_desc = dev::smem_desc_sw128(
+                                b_addr + lo_offset + kk * Shape::kMmaK * kSwizzleBytes,
+                                Shape::kBlockK * kSwizzleBytes, 1024);
+                        }
+                        const uint64_t a_lo_desc =
+                            dev::smem_desc_sw128(a_addr + lo_offset + kk * 32, 16, 1024);
+                        // Small cross terms first, then the leading product.
+                        dev::mma_ss<kKind>(d_tmem, a_lo_desc, b_desc, kIdesc, accumulate);
+                        dev::mma_ss<kKind>(d_tmem, a_desc, b_lo_desc, kIdesc, 1u);
+                        dev::mma_ss<kKind>(d_tmem, a_desc, b_desc, kIdesc, 1u);
+                    } else {
+                        dev::mma_ss<kKind>(d_tmem, a_desc, b_desc, kIdesc, accumulate);
+                    }
+                }
+                dev::tc_commit(empty_bar(stage));
+                if (++stage == kStages) {
+                    stage = 0;
+                    phase ^= 1u;
+                }
+            }
+            if (!ok) {
+                break;
+            }
+            dev::tc_commit(tfull_bar(acc));
+        }
+        if (!ok) {
+            // Drain: the commit arrives once every MMA issued so far has completed, so no
+            // MMA still reads shared memory or writes TMEM when the CTA tears down.
+            dev::tc_commit(drain_bar);
+            dev::mbar_wait(drain_bar, 0, p.status);
+        }
+    } else if (warp >= 4 && warp < 8) {
+        // ---------------- epilogue ----------------
+        const int quarter = warp & 3;
+        const int row_in_tile = quarter * 32 + lane;
+        int local = 0;
+        for (int tile = blockIdx.x; tile < p.total_tiles; tile += gridDim.x, ++local) {
+            const int entry = tile / per_entry;
+            const int rest = tile - entry * per_entry;
+            const int m_block = rest / p.n_tiles;
+            const int n_block = rest - m_block * p.n_tiles;
+            int index, outer;
+            batch_coords(entry, p.inner, index, outer);
+            const int acc = local & 1;
+            const uint32_t acc_phase = (local >> 1) & 1;
+            if (!dev::mbar_wait(tfull_bar(acc), acc_phase, p.status)) {
+                break;
+            }
+            dev::tc_fence_after();
+            const int row = m_block * kBlockM + row_in_tile;
+            const bool row_ok = row < p.m;
+            const long long row_offset = static_cast<long long>(outer) * p.outer_stride_c +
+                                         static_cast<long long>(index) * p.stride_c +
+                                         static_cast<long long>(row) * p.ldc;
+#pragma unroll 1
+            for (int chunk = 0; chunk < BN / 32; ++chunk) {
+                __syncwarp();
+                uint32_t raw[32];
+                const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
+                                       static_cast<uint32_t>(acc * BN + chunk * 32);
+                dev::tmem_load_32(taddr, raw);
+                dev::tmem_wait_load();
+                const int col0 = n_block * BN + chunk * 32;
+                if (row_ok && col0 < p.n) {
+                float v[32];
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    v[j] = p.alpha * __uint_as_float(raw[j]);
+                }
+                if (p.bias != nullptr) {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        if (col0 + j < p.n) {
+                            v[j] += __ldg(p.bias + col0 + j);
+                        }
+                    }
+                }
+                if (p.gelu) {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        v[j] = dev::gelu_erf(v[j]);
+                    }
+                }
+                const bool whole = p.c_vector_ok && (col0 + 32 <= p.n);
+                if (!p.c_bf16) {
+                    float* const out = static_cast<float*>(p.c) + row_offset + col0;
+                    if (whole) {
+                        float4* const out4 = reinterpret_cast<float4*>(out);
+#pragma unroll
+                        for (int q = 0; q < 8; ++q) {
+                            float4 value = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2],
+                                                       v[4 * q + 3]);
+                            if (p.accumulate) {
+                                const float4 old = out4[q];
+                                value.x = old.x + value.x;
+                                value.y = old.y + value.y;
+                                value.z = old.z + value.z;
+                                value.w = old.w + value.w;
+                            }
+                            out4[q] = value;
+                        }
+                    } else {
+                        for (int j = 0; j < 32 && col0 + j < p.n; ++j) {
+                            out[j] = p.accumulate ? out[j] + v[j] : v[j];
+                        }
+                    }
+                } else {
+                    __nv_bfloat16* const out =
+                        static_cast<__nv_bfloat16*>(p.c) + row_offset + col0;
+                    if (whole) {
+                        uint4* const out4 = reinterpret_cast<uint4*>(out);
+#pragma unroll
+                        for (int q = 0; q < 4; ++q) {
+                            float w[8];
+#pragma unroll
+                            for (int j = 0; j < 8; ++j) {
+                                w[j] = v[8 * q + j];
+                            }
+                            if (p.accumulate) {
+                                const uint4 old = out4[q];
+                                const __nv_bfloat162* const pairs =
+                                    reinterpret_cast<const __nv_bfloat162*>(&old);
+#pragma unroll
+                                for (int j = 0; j < 4; ++j) {
+                                    const float2 f = __bfloat1622float2(pairs[j]);
+                                    w[2 * j] = f.x + w[2 * j];
+                                    w[2 * j + 1] = f.y + w[2 * j + 1];
+                                }
+                            }
+                            out4[q] = make_uint4(dev::pack_bf16x2(w[0], w[1]),
+                                                 dev::pack_bf16x2(w[2], w[3]),
+                                                 dev::pack_bf16x2(w[4], w[5]),
+                                                 dev::pack_bf16x2(w[6], w[7]));
+                        }
+                    } else {
+                        for (int j = 0; j < 32 && col0 + j < p.n; ++j) {
+                            const float old = p.accumulate ? __bfloat162float(out[j]) : 0.0F;
+                            out[j] = __float2bfloat16_rn(p.accumulate ? old + v[j] : v[j]);
+                        }
+                    }
+                }
+                }
+            }
+            dev::tc_fence_before();
+            dev::mbar_arrive(tempty_bar(acc));
+        }
+    } else if (Split && warp >= 8) {
+        // ---------------- 3xTF32 splitter ----------------
+        const int t = threadIdx.x - 256;
+        int stage = 0;
+        uint32_t phase = 0;
+        const int total_blocks =
+            ((p.total_tiles - static_cast<int>(blockIdx.x) + static_cast<int>(gridDim.x) - 1) /
+             static_cast<int>(gridDim.x)) *
+            p.k_blocks;
+        for (int step = 0; step < total_blocks; ++step) {
+            if (!dev::mbar_wait(full_bar(stage), phase, p.status)) {
+                break;
+            }
+            float4* const hi = reinterpret_cast<float4*>(smem + (stage_a(stage) - base));
+            float4* const lo =
+                reinterpret_cast<float4*>(smem + (stage_a(stage) - base) + Shape::kABytes +
+                                          Shape::kBBytes);
+            constexpr int kVectors = (Shape::kABytes + Shape::kBBytes) / 16;
+#pragma unroll 4
+            for (int i = t; i < kVectors; i += 128) {
+                const float4 x = hi[i];
+                float4 h;
+                h.x = round_to_tf32(x.x);
+                h.y = round_to_tf32(x.y);
+                h.z = round_to_tf32(x.z);
+                h.w = round_to_tf32(x.w);
+                float4 l;
+                l.x = isfinite(x.x) ? x.x - h.x : 0.0F;
+                l.y = isfinite(x.y) ? x.y - h.y : 0.0F;
+                l.z = isfinite(x.z) ? x.z - h.z : 0.0F;
+                l.w = isfinite(x.w) ? x.w - h.w : 0.0F;
+                hi[i] = h;
+                lo[i] = l;
+            }
+            dev::fence_proxy_async_shared();
+            dev::mbar_arrive(conv_bar(stage));
+            if (++stage == kStages) {
+                stage = 0;
+                phase ^= 1u;
+            }
+        }
+    }
+
+    __syncthreads();
+    if (warp == 2) {
+        dev::tc_fence_after();
+        dev::tmem_dealloc(tmem_base, Shape::kTmemColumns);
+    }
+}
+
+} // namespace cuvit::gemm

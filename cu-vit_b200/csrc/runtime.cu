@@ -1,0 +1,238 @@
+#include "runtime.hpp"
+
+#include "ptx.cuh"
+
+#include <atomic>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+namespace cuvit::host {
+namespace {
+
+thread_local std::string t_last_error;
+std::atomic<long long> g_launches{0};
+
+// The device status word. One per device that loads this library; kernels receive its
+// device address (from cudaGetSymbolAddress) and set bits when a bounded wait expires.
+__device__ unsigned g_device_status;
+
+constexpr int kMaxDevices = 64;
+DeviceContext g_contexts[kMaxDevices];
+std::once_flag g_context_once[kMaxDevices];
+int g_context_status[kMaxDevices];
+
+// One thread waits on an mbarrier that nothing ever arrives on; the bounded wait gives up
+// after limit_ns, sets the status bit and the kernel returns normally.
+__global__ void bounded_wait_selftest_kernel(unsigned* status, unsigned long long limit_ns) {
+    __shared__ __align__(8) unsigned long long barrier;
+    const uint32_t bar = cuvit::dev::smem_u32(&barrier);
+    cuvit::dev::mbar_init(bar, 1);
+    cuvit::dev::fence_barrier_init();
+    cuvit::dev::mbar_wait(bar, 0, status, limit_ns);
+}
+
+int init_context(int device, DeviceContext* context) {
+    cudaDeviceProp properties{};
+    CUVIT_TRY_CUDA(cudaGetDeviceProperties(&properties, device));
+    context->device = device;
+    context->sm_count = properties.multiProcessorCount;
+    context->major = properties.major;
+    context->minor = properties.minor;
+    context->max_smem_optin = properties.sharedMemPerBlockOptin;
+    void* address = nullptr;
+    CUVIT_TRY_CUDA(cudaGetSymbolAddress(&address, g_device_status));
+    context->status = static_cast<unsigned*>(address);
+    CUVIT_TRY_CUDA(cudaMemset(context->status, 0, sizeof(unsigned)));
+    CUVIT_TRY_CUDA(cudaDeviceSynchronize());
+    return CUVIT_OK;
+}
+
+} // namespace
+
+int fail(int status, const std::string& message) {
+    t_last_error = message;
+    return status;
+}
+
+void clear_error() { t_last_error.clear(); }
+
+int check_cuda(cudaError_t error, const char* what) {
+    if (error == cudaSuccess) {
+        return CUVIT_OK;
+    }
+    return fail(error == cudaErrorMemoryAllocation ? CUVIT_OUT_OF_MEMORY : CUVIT_CUDA_ERROR,
+                std::string("CUDA call failed: ") + what + " (" + cudaGetErrorName(error) + ": " +
+                    cudaGetErrorString(error) + ")");
+}
+
+int after_launch(const char* kernel) {
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    const cudaError_t error = cudaGetLastError();
+    if (error != cudaSuccess) {
+        return fail(CUVIT_CUDA_ERROR, std::string("launch of ") + kernel + " failed (" +
+                                          cudaGetErrorName(error) + ": " +
+                                          cudaGetErrorString(error) + ")");
+    }
+    return CUVIT_OK;
+}
+
+int current_context(const DeviceContext** context) {
+    int device = 0;
+    CUVIT_TRY_CUDA(cudaGetDevice(&device));
+    if (device < 0 || device >= kMaxDevices) {
+        return fail(CUVIT_UNSUPPORTED, "device ordinal out of range");
+    }
+    std::call_once(g_context_once[device], [device]() {
+        g_context_status[device] = init_context(device, &g_contexts[device]);
+    });
+    if (g_context_status[device] != CUVIT_OK) {
+        return fail(g_context_status[device], "device context initialisation failed");
+    }
+    *context = &g_contexts[device];
+    return CUVIT_OK;
+}
+
+bool is_blackwell(const DeviceContext& context) { return context.major == 10; }
+
+int tensor_map_encoder(TensorMapEncodeFn* function) {
+    static TensorMapEncodeFn cached = nullptr;
+    static std::once_flag once;
+    static int status = CUVIT_OK;
+    std::call_once(once, []() {
+        void* entry = nullptr;
+        cudaDriverEntryPointQueryResult query{};
+        const cudaError_t error =
+            cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &entry, cudaEnableDefault, &query);
+        if (error != cudaSuccess || query != cudaDriverEntryPointSuccess || entry == nullptr) {
+            status = CUVIT_UNSUPPORTED;
+            return;
+        }
+        cached = reinterpret_cast<TensorMapEncodeFn>(entry);
+    });
+    if (status != CUVIT_OK) {
+        return fail(status, "cuTensorMapEncodeTiled is not available from the driver");
+    }
+    *function = cached;
+    return CUVIT_OK;
+}
+
+bool tma_describable(const TmaTensor& tensor) {
+    const auto base = reinterpret_cast<uintptr_t>(tensor.base);
+    if (base % 16 != 0 || tensor.rank < 1 || tensor.rank > 4) {
+        return false;
+    }
+    for (int dim = 0; dim < tensor.rank; ++dim) {
+        if (tensor.dims[dim] == 0 || tensor.dims[dim] >= (1ull << 32)) {
+            return false;
+        }
+        if (tensor.box[dim] == 0 || tensor.box[dim] > 256) {
+            return false;
+        }
+    }
+    for (int dim = 0; dim + 1 < tensor.rank; ++dim) {
+        const uint64_t stride = tensor.strides_bytes[dim];
+        if (stride == 0 || stride % 16 != 0 || stride >= (1ull << 40)) {
+            return false;
+        }
+    }
+    const uint64_t inner_bytes = static_cast<uint64_t>(tensor.box[0]) * tensor.element_bytes;
+    return inner_bytes % 16 == 0 && inner_bytes <= 128;
+}
+
+int encode_tma(const TmaTensor& tensor, CUtensorMap* map) {
+    if (!tma_describable(tensor)) {
+        return fail(CUVIT_INVALID_ARGUMENT, "tensor cannot be described by a TMA descriptor");
+    }
+    TensorMapEncodeFn encode = nullptr;
+    CUVIT_TRY(tensor_map_encoder(&encode));
+    cuuint64_t dims[4];
+    cuuint64_t strides[3];
+    cuuint32_t box[4];
+    cuuint32_t element_strides[4] = {1, 1, 1, 1};
+    for (int dim = 0; dim < tensor.rank; ++dim) {
+        dims[dim] = tensor.dims[dim];
+        box[dim] = tensor.box[dim];
+    }
+    for (int dim = 0; dim + 1 < tensor.rank; ++dim) {
+        strides[dim] = tensor.strides_bytes[dim];
+    }
+    std::memset(map, 0, sizeof(*map));
+    const CUresult result =
+        encode(map, tensor.type, static_cast<cuuint32_t>(tensor.rank),
+               const_cast<void*>(tensor.base), dims, strides, box, element_strides,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (result != CUDA_SUCCESS) {
+        return fail(CUVIT_CUDA_ERROR,
+                    "cuTensorMapEncodeTiled failed with CUresult " + std::to_string(result));
+    }
+    return CUVIT_OK;
+}
+
+} // namespace cuvit::host
+
+using namespace cuvit::host;
+
+extern "C" {
+
+const char* cuvit_status_string(int status) {
+    switch (status) {
+    case CUVIT_OK:
+        return "ok";
+    case CUVIT_INVALID_ARGUMENT:
+        return "invalid argument";
+    case CUVIT_LENGTH_ERROR:
+        return "length error";
+    case CUVIT_CUDA_ERROR:
+        return "CUDA error";
+    case CUVIT_DEVICE_TIMEOUT:
+        return "device-side wait timed out";
+    case CUVIT_UNSUPPORTED:
+        return "unsupported";
+    case CUVIT_RUNTIME_ERROR:
+        return "runtime error";
+    case CUVIT_OUT_OF_MEMORY:
+        return "out of memory";
+    default:
+        return "unknown status";
+    }
+}
+
+const char* cuvit_last_error_message(void) { return t_last_error.c_str(); }
+
+int cuvit_version(void) { return 100; }
+
+int cuvit_device_status(unsigned* flags) {
+    if (flags == nullptr) {
+        return fail(CUVIT_INVALID_ARGUMENT, "flags cannot be null");
+    }
+    const DeviceContext* context = nullptr;
+    CUVIT_TRY(current_context(&context));
+    CUVIT_TRY_CUDA(cudaDeviceSynchronize());
+    unsigned value = 0;
+    CUVIT_TRY_CUDA(cudaMemcpy(&value, context->status, sizeof(value), cudaMemcpyDeviceToHost));
+    if (value != 0) {
+        CUVIT_TRY_CUDA(cudaMemset(context->status, 0, sizeof(unsigned)));
+        CUVIT_TRY_CUDA(cudaDeviceSynchronize());
+    }
+    *flags = value;
+    if (value & cuvit::dev::kStatusTimeout) {
+        return fail(CUVIT_DEVICE_TIMEOUT, "a kernel gave up on a bounded device-side wait");
+    }
+    return CUVIT_OK;
+}
+
+long long cuvit_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
+
+int cuvit_selftest_bounded_wait(unsigned long long limit_ns) {
+    if (limit_ns == 0 || limit_ns > 1000000000ull) {
+        return fail(CUVIT_INVALID_ARGUMENT, "self-test wait limit must be in (0, 1 s]");
+    }
+    const DeviceContext* context = nullptr;
+    CUVIT_TRY(current_context(&context));
+    bounded_wait_selftest_kernel<<<1, 1>>>(context->status, limit_ns);
+    return after_launch("bounded_wait_selftest_kernel");
+}
+
+} // extern "C"

@@ -1,0 +1,84 @@
+// Host-side plumbing shared by every operator: status codes with a per-thread detail
+// message, the per-device context (SM count, device status word, the driver's tensor-map
+// encoder), and helpers to encode TMA descriptors.
+#pragma once
+
+#include "cuvit_b200.h"
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <string>
+
+namespace cuvit::host {
+
+// Records a detail message for the calling thread and returns the status unchanged.
+int fail(int status, const std::string& message);
+// Turns a CUDA error into CUVIT_CUDA_ERROR with the call text; CUVIT_OK on success.
+int check_cuda(cudaError_t error, const char* what);
+void clear_error();
+
+#define CUVIT_TRY_CUDA(expression)                                                                 \
+    do {                                                                                           \
+        const int cuvit_try_status_ = ::cuvit::host::check_cuda((expression), #expression);       \
+        if (cuvit_try_status_ != CUVIT_OK) {                                                       \
+            return cuvit_try_status_;                                                              \
+        }                                                                                          \
+    } while (0)
+
+#define CUVIT_TRY(expression)                                                                      \
+    do {                                                                                           \
+        const int cuvit_try_status_ = (expression);                                                \
+        if (cuvit_try_status_ != CUVIT_OK) {                                                       \
+            return cuvit_try_status_;                                                              \
+        }                                                                                          \
+    } while (0)
+
+// After a launch: map cudaGetLastError() to a status and count the launch.
+int after_launch(const char* kernel);
+
+struct DeviceContext {
+    int device = -1;
+    int sm_count = 0;
+    int major = 0;
+    int minor = 0;
+    size_t max_smem_optin = 0;
+    unsigned* status = nullptr; // device address of the status word
+};
+
+// Context of the current device, initialised on first use (thread-safe).
+int current_context(const DeviceContext** context);
+
+// True for sm_100 parts, where the tcgen05 kernels can run.
+bool is_blackwell(const DeviceContext& context);
+
+using TensorMapEncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                       const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                       const cuuint32_t*, CUtensorMapInterleave,
+                                       CUtensorMapSwizzle, CUtensorMapL2promotion,
+                                       CUtensorMapFloatOOBfill);
+
+// cuTensorMapEncodeTiled from the driver, fetched through the runtime's entry-point query.
+int tensor_map_encoder(TensorMapEncodeFn* function);
+
+// A strided tensor of up to 4 dimensions, innermost first. strides_bytes[i] is the distance
+// between consecutive indices of dimension i+1.
+struct TmaTensor {
+    const void* base = nullptr;
+    CUtensorMapDataType type = CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+    int element_bytes = 4;
+    int rank = 2;
+    uint64_t dims[4] = {1, 1, 1, 1};
+    uint64_t strides_bytes[3] = {0, 0, 0};
+    uint32_t box[4] = {1, 1, 1, 1};
+};
+
+// Whether TMA can describe the tensor: 16-byte aligned base, strides multiples of 16 bytes
+// and below 2^40, extents below 2^32, box inner extent of at most 128 bytes.
+bool tma_describable(const TmaTensor& tensor);
+
+// Encodes a 128-byte-swizzled tiled descriptor (zero fill out of bounds).
+int encode_tma(const TmaTensor& tensor, CUtensorMap* map);
+
+} // namespace cuvit::host

@@ -1,0 +1,80 @@
+"""The fused attention kernel against the oracle's restatement of the reference's attention
+(tests/reference/vit.hpp:149-183: Q.K^T * scale -> softmax -> .V per head).
+
+BF16 runs on bf16-rounded projections, so the remaining error is P rounded to bf16 (2^-9
+relative) plus the bf16 output store (2^-9): bounded by 1e-2 of the largest |V| of the head.
+TF32 rounds Q, K, P and V to 10-bit mantissas: the same bound holds with room to spare.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+import oracle
+from cuvit import kernels
+from helpers import bf16_round, to_device, to_host
+
+pytestmark = pytest.mark.gpu
+
+
+def run_attention(qkv, batch, tokens, heads, dtype, torch):
+    e = heads * 64
+    torch_dtype = torch.bfloat16 if dtype == kernels.DTYPE_BF16 else torch.float32
+    dq = to_device(qkv, torch_dtype)
+    out = torch.full((batch * tokens * e,), float("nan"), dtype=torch_dtype, device="cuda")
+    kernels.launch_attention(dq, out, dtype, batch, tokens, heads, 64, 0.125)
+    torch.cuda.synchronize()
+    return to_host(out).reshape(batch, tokens, e)
+
+
+def expected(qkv, batch, tokens, heads):
+    e = heads * 64
+    per_image = qkv.reshape(batch, tokens * 3 * e)
+    return np.stack([oracle.attention(per_image[b], tokens, e, heads).reshape(tokens, e)
+                     for b in range(batch)])
+
+
+@pytest.mark.parametrize("dtype", [kernels.DTYPE_BF16, kernels.DTYPE_F32], ids=["bf16", "tf32"])
+@pytest.mark.parametrize("batch,tokens,heads", [(1, 1, 1), (2, 17, 2), (1, 64, 3), (3, 128, 2),
+                                                (2, 129, 1), (2, 197, 3), (1, 197, 12),
+                                                (1, 256, 2), (4, 50, 16)])
+def test_fused_attention_matches_reference_attention(dtype, batch, tokens, heads, cuda):
+    rng = np.random.default_rng(tokens * 13 + heads + batch)
+    qkv = rng.standard_normal(batch * tokens * 3 * heads * 64).astype(np.float32)
+    if dtype == kernels.DTYPE_BF16:
+        qkv = bf16_round(qkv)
+    got = run_attention(qkv, batch, tokens, heads, dtype, cuda)
+    want = expected(qkv, batch, tokens, heads)
+    assert np.isfinite(got).all(), "rows beyond the token count leaked into the output"
+    v_max = np.abs(qkv.reshape(batch, tokens, 3, heads * 64)[:, :, 2]).max()
+    err = np.abs(got - want).max()
+    assert err <= 1e-2 * v_max, f"max error {err:.3g} vs bound {1e-2 * v_max:.3g}"
+
+
+def test_fused_attention_sharp_and_flat_rows(cuda):
+    """Large logits (near one-hot softmax) and all-equal keys (uniform softmax)."""
+    batch, tokens, heads = 1, 197, 2
+    e = heads * 64
+    rng = np.random.default_rng(3)
+    qkv = rng.standard_normal((batch, tokens, 3, e)).astype(np.float32)
+    qkv[:, :, 0] *= 6.0  # logits of order 6*sqrt(64)/8 * |k|: sharp
+    qkv[:, :60, 1] = qkv[:, 0:1, 1]  # 60 identical keys
+    qkv = bf16_round(qkv.reshape(-1))
+    for dtype in (kernels.DTYPE_BF16, kernels.DTYPE_F32):
+        got = run_attention(qkv, batch, tokens, heads, dtype, cuda)
+        want = expected(qkv, batch, tokens, heads)
+        v_max = np.abs(qkv.reshape(batch, tokens, 3, e)[:, :, 2]).max()
+        assert np.abs(got - want).max() <= 1.5e-2 * v_max
+
+
+def test_fused_attention_is_deterministic_and_batch_invariant(cuda):
+    batch, tokens, heads = 4, 197, 3
+    qkv = bf16_round(np.random.default_rng(11).standard_normal(batch * tokens * 3 * heads * 64))
+    first = run_attention(qkv, batch, tokens, heads, kernels.DTYPE_BF16, cuda)
+    second = run_attention(qkv, batch, tokens, heads, kernels.DTYPE_BF16, cuda)
+    np.testing.assert_array_equal(first, second)
+    per_image = qkv.reshape(batch, -1)
+    for b in range(batch):
+        alone = run_attention(per_image[b], 1, tokens, heads, kernels.DTYPE_BF16, cuda)
+        np.testing.assert_array_equal(alone[0], first[b])

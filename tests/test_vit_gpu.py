@@ -1,0 +1,207 @@
+"""The model runner on the GPU: logits against the reference's own CPU code (golden vectors)
+and the oracle, the properties tests/vit_test.cu pins (determinism, batch invariance,
+partial batches, limits, memory), and the BASELINE configurations at full size.
+
+Tolerances (max-abs on logits unless noted):
+  FP32 path   rtol 1e-4 + atol 1e-4, the reference's own (tests/vit_test.cu:125-130)
+  TF32 path   1e-3 max-abs
+  BF16 path   3e-2 max-abs and identical top-1
+"""
+
+from __future__ import annotations
+
+import pathlib
+import tempfile
+
+import numpy as np
+import pytest
+
+import make_golden as mg
+import oracle
+from cuvit import VisionTransformer, cvw
+from cuvit.errors import InvalidArgument
+from cuvit.vit import (PRECISION_BF16, PRECISION_FP32, PRECISION_TF32, VitConfig,
+                       random_weights, tensor_specs)
+from helpers import assert_close, to_device, to_host
+
+pytestmark = pytest.mark.gpu
+
+TF32_TOL = 1e-3
+BF16_TOL = 3e-2
+
+
+def golden_case(label):
+    return next(c for c in mg.VIT_CASES if c[0] == label)
+
+
+def model_logits(model, images, batch, torch, graph=False):
+    d_images = to_device(images)
+    d_logits = torch.full((batch, model.config.classes), float("nan"), device="cuda")
+    if graph:
+        model.forward_graph(d_images, d_logits, batch)
+    else:
+        model.forward(d_images, d_logits, batch)
+    torch.cuda.synchronize()
+    return to_host(d_logits)
+
+
+@pytest.mark.parametrize("label,precisions", [
+    ("vit small", [PRECISION_FP32]),
+    ("vit hd64", [PRECISION_FP32, PRECISION_TF32, PRECISION_BF16]),
+    ("vit tiny", [PRECISION_FP32, PRECISION_TF32, PRECISION_BF16]),
+])
+def test_logits_match_reference_golden(label, precisions, golden, cuda):
+    _, config, weight_seed, std, count, image_seed = golden_case(label)
+    weights = random_weights(config, weight_seed, std=std)
+    images = mg.vit_images(config, count, image_seed)
+    want = golden[f"vit/{label}/logits"]
+    for precision in precisions:
+        model = VisionTransformer(config, weights, max_batch=count, precision=precision)
+        got = model_logits(model, images, count, cuda)
+        if precision == PRECISION_FP32:
+            assert_close(got, want, 1e-4, 1e-4, f"{label} FP32")
+        elif precision == PRECISION_TF32:
+            assert np.abs(got - want).max() <= TF32_TOL, f"{label} TF32 {np.abs(got-want).max()}"
+        else:
+            assert np.abs(got - want).max() <= BF16_TOL, f"{label} BF16 {np.abs(got-want).max()}"
+            assert (got.argmax(1) == want.argmax(1)).all()
+        model.close()
+
+
+@pytest.mark.parametrize("precision", [PRECISION_FP32, PRECISION_BF16], ids=["fp32", "bf16"])
+def test_forward_is_deterministic_and_batch_invariant(precision, cuda):
+    """tests/vit_test.cu:134-149 and :203-238 -- bitwise."""
+    _, config, weight_seed, std, _, _ = golden_case("vit hd64")
+    weights = random_weights(config, 606, std=std)
+    batch = 5
+    images = mg.vit_images(config, batch, 100)
+    batched = VisionTransformer(config, weights, max_batch=batch, precision=precision)
+    single = VisionTransformer(config, weights, max_batch=1, precision=precision)
+    together = model_logits(batched, images, batch, cuda)
+    again = model_logits(batched, images, batch, cuda)
+    np.testing.assert_array_equal(together, again)
+    per_image = config.image_elements()
+    for i in range(batch):
+        alone = model_logits(single, images[i * per_image:(i + 1) * per_image], 1, cuda)
+        np.testing.assert_array_equal(alone[0], together[i])
+    assert (together[0] != together[1]).any(), "different images produced identical logits"
+
+
+def test_partial_batch_is_clean_and_graph_matches_eager(cuda):
+    """tests/vit_test.cu:242-266; graph replay must equal the eager pass bitwise."""
+    _, config, _, std, _, _ = golden_case("vit hd64")
+    weights = random_weights(config, 707, std=std)
+    model = VisionTransformer(config, weights, max_batch=4, precision=PRECISION_BF16)
+    pair = mg.vit_images(config, 2, 21)
+    four = np.concatenate([pair, pair])
+    full = model_logits(model, four, 4, cuda)
+    two = model_logits(model, pair, 2, cuda)
+    np.testing.assert_array_equal(two, full[:2])
+    graph = model_logits(model, four, 4, cuda, graph=True)
+    np.testing.assert_array_equal(graph, full)
+    host = model.forward_host(four)
+    np.testing.assert_array_equal(host, full)
+
+
+def test_limits_and_memory(cuda):
+    _, config, _, std, _, _ = golden_case("vit small")
+    weights = random_weights(config, 808, std=std)
+    model = VisionTransformer(config, weights, max_batch=2, precision=PRECISION_FP32)
+    per_image = model.image_elements()
+    with pytest.raises(InvalidArgument):
+        model.forward_host(np.zeros(per_image * 3, np.float32))
+    with pytest.raises(ValueError):
+        model.forward_host(np.zeros(per_image + 1, np.float32))
+    assert model.weight_bytes() > 0 and model.activation_bytes() > 0
+    deeper = VitConfig(**{**config.__dict__, "depth": config.depth * 4})
+    deep = VisionTransformer(deeper, random_weights(deeper, 6), max_batch=2,
+                             precision=PRECISION_FP32)
+    assert deep.activation_bytes() == model.activation_bytes()
+    assert deep.weight_bytes() > model.weight_bytes()
+    one = VisionTransformer(config, weights, max_batch=1, precision=PRECISION_FP32)
+    eight = VisionTransformer(config, weights, max_batch=8, precision=PRECISION_FP32)
+    assert eight.weight_bytes() == one.weight_bytes()
+    assert one.activation_bytes() < eight.activation_bytes() <= 8 * one.activation_bytes()
+
+
+def test_weight_file_path_matches_host_path(cuda):
+    _, config, weight_seed, std, count, image_seed = golden_case("vit hd64")
+    weights = random_weights(config, weight_seed, std=std)
+    images = mg.vit_images(config, count, image_seed)
+    with tempfile.TemporaryDirectory() as tmp:
+        path = pathlib.Path(tmp) / "w.cvw"
+        writer = cvw.WeightFileWriter()
+        for name, extents in tensor_specs(config):
+            writer.add(name, extents, weights[name])
+        writer.write(path)
+        from_file = VisionTransformer.from_file(config, path, max_batch=count,
+                                                precision=PRECISION_BF16)
+        from_host = VisionTransformer(config, cvw.WeightFile.load(path), max_batch=count,
+                                      precision=PRECISION_BF16)
+        np.testing.assert_array_equal(model_logits(from_file, images, count, cuda),
+                                      model_logits(from_host, images, count, cuda))
+
+
+@pytest.mark.skipif(not oracle.ref_gpu_available(), reason="oracle/_ref GPU library not built")
+def test_tf32_path_against_reference_fp32_gpu_path(cuda):
+    """the TF32 path within 1e-3 of the reference's own FP32 GPU path
+    (src/model/vit.cu built for sm_100a, oracle/_ref), ViT-Tiny/16, 4 images."""
+    import ctypes
+
+    config = VitConfig()
+    weights = random_weights(config, 1)
+    batch = 4
+    images = mg.vit_images(config, batch, 1)
+    with tempfile.TemporaryDirectory() as tmp:
+        path = pathlib.Path(tmp) / "tiny.cvw"
+        writer = cvw.WeightFileWriter()
+        for name, extents in tensor_specs(config):
+            writer.add(name, extents, weights[name])
+        writer.write(path)
+        ref = oracle.ref_gpu()
+        ints = oracle.config_ints(config)
+        handle = ref.ref_gpu_vit_create(str(path).encode(), ints.ctypes.data, 1e-6, batch)
+        assert handle
+        d_images = to_device(images)
+        d_logits = to_device(np.zeros(batch * config.classes))
+        assert ref.ref_gpu_vit_forward(handle, ctypes.c_void_p(d_images.data_ptr()),
+                                       ctypes.c_void_p(d_logits.data_ptr()), batch, None) == 0
+        cuda.cuda.synchronize()
+        reference = to_host(d_logits).reshape(batch, -1)
+        ref.ref_gpu_vit_destroy(handle)
+    ours = VisionTransformer(config, weights, max_batch=batch, precision=PRECISION_TF32)
+    got = model_logits(ours, images, batch, cuda)
+    assert np.abs(got - reference).max() <= TF32_TOL
+    cpu = oracle.vit_forward(config, weights, tensor_specs(config), images)
+    assert np.abs(got - cpu).max() <= TF32_TOL
+    assert np.abs(reference - cpu).max() <= 1e-4
+
+
+# BASELINE configs 2-4 at full batch; the oracle checks a sample of images (first, second,
+# last two) -- which also proves batch indexing at the far end -- and every logit is finite.
+FULL = [
+    ("vit-ti b32 tf32", VitConfig(), 32, PRECISION_TF32, 1, TF32_TOL),
+    ("vit-s b128 bf16", VitConfig(embed_dim=384, heads=6, mlp_hidden=1536), 128,
+     PRECISION_BF16, 2, BF16_TOL),
+    ("vit-b b256 bf16", VitConfig(embed_dim=768, heads=12, mlp_hidden=3072), 256,
+     PRECISION_BF16, 3, BF16_TOL),
+]
+
+
+@pytest.mark.parametrize("label,config,batch,precision,seed,tol", FULL,
+                         ids=[f[0] for f in FULL])
+def test_baseline_configs_full_batch(label, config, batch, precision, seed, tol, cuda):
+    weights = random_weights(config, seed)
+    rng = np.random.default_rng(seed)
+    images = rng.standard_normal(batch * config.image_elements()).astype(np.float32)
+    model = VisionTransformer(config, weights, max_batch=batch, precision=precision)
+    got = model_logits(model, images, batch, cuda)
+    assert np.isfinite(got).all()
+    sample = np.array([0, 1, batch - 2, batch - 1])
+    per_image = config.image_elements()
+    picked = np.concatenate([images[i * per_image:(i + 1) * per_image] for i in sample])
+    want = oracle.vit_forward(config, weights, tensor_specs(config), picked)
+    err = np.abs(got[sample] - want).max()
+    assert err <= tol, f"{label}: max-abs logit error {err:.3g}"
+    assert (got[sample].argmax(1) == want.argmax(1)).all(), f"{label}: top-1 differs"
+    model.close()
