@@ -864,6 +864,11 @@ int cuvit_vit_forward_graph(cuvit_vit* model, const float* images, float* logits
     const auto key = std::make_tuple(batch, images, logits);
     auto found = model->graphs.find(key);
     if (found == model->graphs.end()) {
+        // One eager pass first, so every one-time set-up (device context, kernel attributes,
+        // the driver's tensor-map entry point) happens outside the capture, where device
+        // synchronisation is allowed.
+        CUVIT_TRY(run_forward(*model, images, logits, batch, model->capture_stream));
+        CUVIT_TRY_CUDA(cudaStreamSynchronize(model->capture_stream));
         // Capture on the model's own stream: the caller's may be the legacy default stream,
         // which cannot be captured.
         CUVIT_TRY_CUDA(cudaStreamBeginCapture(model->capture_stream,
