@@ -40,6 +40,7 @@ struct Params {
     float scale_log2; // scale * log2(e)
     float scale;
     void* context;
+    int round_output; // FP32 path: store the context rounded to TF32 values
     unsigned* status;
 };
 
@@ -58,11 +59,16 @@ struct Layout {
 template <int ElemBytes>
 __global__ void __launch_bounds__(kThreads)
     attention_kernel(const __grid_constant__ CUtensorMap map_q,
-                     const __grid_constant__ CUtensorMap map_kv, const Params p) {
+                     const __grid_constant__ CUtensorMap map_kv,
+                     const __grid_constant__ CUtensorMap map_v, const Params p) {
     using L = Layout<ElemBytes>;
     using T = typename std::conditional<ElemBytes == 2, __nv_bfloat16, float>::type;
     constexpr dev::MmaKind kKind = ElemBytes == 2 ? dev::MmaKind::kF16 : dev::MmaKind::kTF32;
     constexpr uint32_t kFormat = ElemBytes == 2 ? 1u : 2u;
+    // V is the MN-major operand of P.V: 32-bit elements need the 32-byte-atom swizzle.
+    constexpr uint32_t kVLayout =
+        ElemBytes == 4 ? dev::kLayoutSwizzle128Atom32 : dev::kLayoutSwizzle128;
+    constexpr uint32_t kVAtomBytes = ElemBytes == 4 ? 512u : 1024u;
 
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw_base = dev::smem_u32(smem_raw);
@@ -109,6 +115,7 @@ __global__ void __launch_bounds__(kThreads)
         // ---------------- loads and MMA issue ----------------
         dev::tma_prefetch_descriptor(&map_q);
         dev::tma_prefetch_descriptor(&map_kv);
+        dev::tma_prefetch_descriptor(&map_v);
         const int hd = p.heads * kHeadDim;
         const uint32_t bytes = static_cast<uint32_t>(p.q_tiles * L::kQTileBytes +
                                                      2 * L::kDAtoms * kv_region);
@@ -124,7 +131,7 @@ __global__ void __launch_bounds__(kThreads)
             const int ck[3] = {hd + head * kHeadDim + j * L::kAtomElems, 0, image};
             dev::tma_load(k_smem + j * kv_region, &map_kv, bar_load, 3, ck);
             const int cv[3] = {2 * hd + head * kHeadDim + j * L::kAtomElems, 0, image};
-            dev::tma_load(v_smem + j * kv_region, &map_kv, bar_load, 3, cv);
+            dev::tma_load(v_smem + j * kv_region, &map_v, bar_load, 3, cv);
         }
         bool ok = dev::mbar_wait(bar_load, 0, p.status);
         const uint32_t idesc_s = dev::make_idesc(kFormat, kTileQ, p.n_keys, false, false);
@@ -157,8 +164,9 @@ __global__ void __launch_bounds__(kThreads)
             const int steps = p.n_keys / L::kMmaK;
             for (int kk = 0; kk < steps; ++kk) {
                 const uint32_t a_tmem = tmem + static_cast<uint32_t>(kk * 8);
-                const uint64_t b_desc = dev::smem_desc_sw128(
-                    v_smem + kk * L::kMmaK * 128, static_cast<uint32_t>(kv_region), 1024);
+                const uint64_t b_desc =
+                    dev::smem_desc(v_smem + kk * L::kMmaK * 128, static_cast<uint32_t>(kv_region),
+                                   kVAtomBytes, kVLayout);
                 dev::mma_ts<kKind>(tmem + L::kOColumn, a_tmem, b_desc, kIdescO,
                                    kk > 0 ? 1u : 0u);
             }
@@ -217,13 +225,17 @@ __global__ void __launch_bounds__(kThreads)
                     }
                     dev::tmem_store_16(tmem + lane_field + c * 16, packed);
                 } else {
+                    // P enters the tensor core as TF32: round it here (the MMA would
+                    // truncate) and normalise by the sum of exactly these values.
                     uint32_t lo[16];
                     uint32_t hi[16];
 #pragma unroll
                     for (int j = 0; j < 16; ++j) {
-                        lo[j] = __float_as_uint(e[j]);
-                        hi[j] = __float_as_uint(e[16 + j]);
-                        sum += e[j] + e[16 + j];
+                        const float a = dev::round_to_tf32(e[j]);
+                        const float b = dev::round_to_tf32(e[16 + j]);
+                        lo[j] = __float_as_uint(a);
+                        hi[j] = __float_as_uint(b);
+                        sum += a + b;
                     }
                     dev::tmem_store_16(tmem + lane_field + c * 32, lo);
                     dev::tmem_store_16(tmem + lane_field + c * 32 + 16, hi);
@@ -273,16 +285,17 @@ __global__ void __launch_bounds__(kThreads)
                     }
                 } else {
                     float4* const out4 = reinterpret_cast<float4*>(out);
+                    const bool round = p.round_output != 0;
+                    const auto finish = [inverse, round](uint32_t raw) {
+                        const float value = __uint_as_float(raw) * inverse;
+                        return round ? dev::round_to_tf32(value) : value;
+                    };
 #pragma unroll
                     for (int q = 0; q < 8; ++q) {
-                        out4[q] = make_float4(__uint_as_float(o0[4 * q]) * inverse,
-                                              __uint_as_float(o0[4 * q + 1]) * inverse,
-                                              __uint_as_float(o0[4 * q + 2]) * inverse,
-                                              __uint_as_float(o0[4 * q + 3]) * inverse);
-                        out4[8 + q] = make_float4(__uint_as_float(o1[4 * q]) * inverse,
-                                                  __uint_as_float(o1[4 * q + 1]) * inverse,
-                                                  __uint_as_float(o1[4 * q + 2]) * inverse,
-                                                  __uint_as_float(o1[4 * q + 3]) * inverse);
+                        out4[q] = make_float4(finish(o0[4 * q]), finish(o0[4 * q + 1]),
+                                              finish(o0[4 * q + 2]), finish(o0[4 * q + 3]));
+                        out4[8 + q] = make_float4(finish(o1[4 * q]), finish(o1[4 * q + 1]),
+                                                  finish(o1[4 * q + 2]), finish(o1[4 * q + 3]));
                     }
                 }
             }
@@ -300,7 +313,7 @@ __global__ void __launch_bounds__(kThreads)
 
 template <int ElemBytes>
 int launch_typed(const void* qkv, void* context, int batch, int tokens, int heads, float scale,
-                 const host::DeviceContext& device, cudaStream_t stream) {
+                 bool round_output, const host::DeviceContext& device, cudaStream_t stream) {
     using L = Layout<ElemBytes>;
     const int n_keys = (tokens + 15) / 16 * 16;
     const int q_tiles = (tokens + kTileQ - 1) / kTileQ;
@@ -321,11 +334,17 @@ int launch_typed(const void* qkv, void* context, int batch, int tokens, int head
     tq.box[2] = 1;
     host::TmaTensor tkv = tq;
     tkv.box[1] = static_cast<uint32_t>(n_keys);
+    host::TmaTensor tv = tkv;
+    if (ElemBytes == 4) {
+        tv.swizzle = CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B;
+    }
 
     CUtensorMap map_q;
     CUtensorMap map_kv;
+    CUtensorMap map_v;
     CUVIT_TRY(host::encode_tma(tq, &map_q));
     CUVIT_TRY(host::encode_tma(tkv, &map_kv));
+    CUVIT_TRY(host::encode_tma(tv, &map_v));
 
     Params params;
     params.tokens = tokens;
@@ -335,6 +354,7 @@ int launch_typed(const void* qkv, void* context, int batch, int tokens, int head
     params.scale = scale;
     params.scale_log2 = scale * 1.4426950408889634F;
     params.context = context;
+    params.round_output = round_output ? 1 : 0;
     params.status = device.status;
 
     int smem = 1024 + q_tiles * L::kQTileBytes + 2 * L::kDAtoms * n_keys * 128 + 64;
@@ -349,7 +369,7 @@ int launch_typed(const void* qkv, void* context, int batch, int tokens, int head
             kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
     });
     CUVIT_TRY_CUDA(attribute_error);
-    kernel<<<batch * heads, kThreads, smem, stream>>>(map_q, map_kv, params);
+    kernel<<<batch * heads, kThreads, smem, stream>>>(map_q, map_kv, map_v, params);
     return host::after_launch("attention_kernel");
 }
 
@@ -368,8 +388,8 @@ extern "C" int cuvit_attention(const void* qkv, void* context, int dtype, int ba
     if (qkv == nullptr || context == nullptr) {
         return fail(CUVIT_INVALID_ARGUMENT, "attention operands cannot be null");
     }
-    if (dtype != CUVIT_DTYPE_BF16 && dtype != CUVIT_DTYPE_F32) {
-        return fail(CUVIT_INVALID_ARGUMENT, "attention data type must be BF16 or F32");
+    if (dtype != CUVIT_DTYPE_BF16 && dtype != CUVIT_DTYPE_F32 && dtype != CUVIT_DTYPE_TF32) {
+        return fail(CUVIT_INVALID_ARGUMENT, "attention data type must be BF16, F32 or TF32");
     }
     if (head_dim != cuvit::attn::kHeadDim || tokens > cuvit::attn::kMaxTokens) {
         return fail(CUVIT_UNSUPPORTED,
@@ -389,7 +409,9 @@ extern "C" int cuvit_attention(const void* qkv, void* context, int dtype, int ba
     }
     const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
     if (dtype == CUVIT_DTYPE_BF16) {
-        return cuvit::attn::launch_typed<2>(qkv, context, batch, tokens, heads, scale, *device, s);
+        return cuvit::attn::launch_typed<2>(qkv, context, batch, tokens, heads, scale, false,
+                                            *device, s);
     }
-    return cuvit::attn::launch_typed<4>(qkv, context, batch, tokens, heads, scale, *device, s);
+    return cuvit::attn::launch_typed<4>(qkv, context, batch, tokens, heads, scale,
+                                        dtype == CUVIT_DTYPE_TF32, *device, s);
 }

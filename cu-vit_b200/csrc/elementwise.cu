@@ -10,6 +10,7 @@
 #include <cuda_bf16.h>
 
 #include <cstdint>
+#include <type_traits>
 
 namespace cuvit::ops {
 namespace {
@@ -54,6 +55,25 @@ __device__ __forceinline__ void store4(__nv_bfloat16* out, float4 value) {
 __device__ __forceinline__ void store1(float* out, float value) { *out = value; }
 __device__ __forceinline__ void store1(__nv_bfloat16* out, float value) {
     *out = __float2bfloat16_rn(value);
+}
+
+// Float storage holding values rounded to the nearest TF32 value (CUVIT_DTYPE_TF32).
+struct Tf32 {
+    float value;
+};
+
+__device__ __forceinline__ void store4(Tf32* out, float4 value) {
+    *reinterpret_cast<float4*>(out) =
+        make_float4(dev::round_to_tf32(value.x), dev::round_to_tf32(value.y),
+                    dev::round_to_tf32(value.z), dev::round_to_tf32(value.w));
+}
+
+__device__ __forceinline__ void store1(Tf32* out, float value) {
+    out->value = dev::round_to_tf32(value);
+}
+
+bool valid_storage(int dtype) {
+    return dtype == CUVIT_DTYPE_F32 || dtype == CUVIT_DTYPE_BF16 || dtype == CUVIT_DTYPE_TF32;
 }
 
 // ---- layer norm ---------------------------------------------------------------------------
@@ -346,6 +366,14 @@ __global__ void convert_bf16_kernel(const float* __restrict__ input,
     }
 }
 
+__global__ void round_tf32_kernel(const float* input, float* output, long long count) {
+    const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+    for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < count;
+         i += stride) {
+        output[i] = dev::round_to_tf32(input[i]);
+    }
+}
+
 // patches[b*P + p][c*pp + r*patch + q] = images[b][c][pr*patch + r][pc*patch + q]
 // (src/kernels/normalization.cu:159-192). Vectorised: 4 consecutive q per thread.
 template <typename Out, int Vec>
@@ -401,7 +429,7 @@ int layer_norm_impl(const float* input, long long in_stride, const float* gamma,
     if (input == nullptr || gamma == nullptr || beta == nullptr || output == nullptr) {
         return host::fail(CUVIT_INVALID_ARGUMENT, "Layer norm operands cannot be null");
     }
-    if (out_dtype != CUVIT_DTYPE_F32 && out_dtype != CUVIT_DTYPE_BF16) {
+    if (!valid_storage(out_dtype)) {
         return host::fail(CUVIT_INVALID_ARGUMENT, "unknown layer norm output type");
     }
     if (in_stride == 0) {
@@ -413,30 +441,28 @@ int layer_norm_impl(const float* input, long long in_stride, const float* gamma,
     if (in_stride < columns || out_stride < columns) {
         return host::fail(CUVIT_INVALID_ARGUMENT, "layer norm row stride is below the row");
     }
-    const bool bf16 = out_dtype == CUVIT_DTYPE_BF16;
-    const int out_bytes = bf16 ? 2 : 4;
+    const int out_bytes = out_dtype == CUVIT_DTYPE_BF16 ? 2 : 4;
     const bool fast = columns % 4 == 0 && columns <= 4 * kWarp * kMaxVec && aligned(input, 16) &&
                       aligned(gamma, 16) && aligned(beta, 16) && in_stride % 4 == 0 &&
                       aligned(output, 4 * out_bytes) && out_stride % 4 == 0;
-    if (fast) {
-        const unsigned blocks = static_cast<unsigned>((rows + kRowsPerBlock - 1) / kRowsPerBlock);
-        if (bf16) {
-            layer_norm_warp_kernel<__nv_bfloat16><<<blocks, kThreads, 0, stream>>>(
-                input, in_stride, gamma, beta, static_cast<__nv_bfloat16*>(output), out_stride,
-                rows, columns, epsilon);
+    const auto run = [&](auto* out) {
+        using Out = std::remove_pointer_t<decltype(out)>;
+        if (fast) {
+            const unsigned blocks =
+                static_cast<unsigned>((rows + kRowsPerBlock - 1) / kRowsPerBlock);
+            layer_norm_warp_kernel<Out><<<blocks, kThreads, 0, stream>>>(
+                input, in_stride, gamma, beta, out, out_stride, rows, columns, epsilon);
         } else {
-            layer_norm_warp_kernel<float><<<blocks, kThreads, 0, stream>>>(
-                input, in_stride, gamma, beta, static_cast<float*>(output), out_stride, rows,
-                columns, epsilon);
+            layer_norm_block_kernel<Out><<<rows, kThreads, 0, stream>>>(
+                input, in_stride, gamma, beta, out, out_stride, columns, epsilon);
         }
-    } else if (bf16) {
-        layer_norm_block_kernel<__nv_bfloat16><<<rows, kThreads, 0, stream>>>(
-            input, in_stride, gamma, beta, static_cast<__nv_bfloat16*>(output), out_stride,
-            columns, epsilon);
+    };
+    if (out_dtype == CUVIT_DTYPE_BF16) {
+        run(static_cast<__nv_bfloat16*>(output));
+    } else if (out_dtype == CUVIT_DTYPE_TF32) {
+        run(static_cast<Tf32*>(output));
     } else {
-        layer_norm_block_kernel<float><<<rows, kThreads, 0, stream>>>(
-            input, in_stride, gamma, beta, static_cast<float*>(output), out_stride, columns,
-            epsilon);
+        run(static_cast<float*>(output));
     }
     return host::after_launch("layer_norm");
 }
@@ -482,7 +508,7 @@ int extract_patches_impl(const float* images, void* patches, int out_dtype, int 
     if (images == nullptr || patches == nullptr) {
         return host::fail(CUVIT_INVALID_ARGUMENT, "Patch extraction operands cannot be null");
     }
-    if (out_dtype != CUVIT_DTYPE_F32 && out_dtype != CUVIT_DTYPE_BF16) {
+    if (!valid_storage(out_dtype)) {
         return host::fail(CUVIT_INVALID_ARGUMENT, "unknown patch output type");
     }
     const int across = width / patch;
@@ -497,24 +523,22 @@ int extract_patches_impl(const float* images, void* patches, int out_dtype, int 
     const bool vec = patch % 4 == 0 && width % 4 == 0 && aligned(images, 16) &&
                      aligned(patches, bf16 ? 8 : 16);
     const unsigned blocks = static_cast<unsigned>(grid);
+    const auto run = [&](auto* out) {
+        using Out = std::remove_pointer_t<decltype(out)>;
+        if (vec) {
+            extract_patches_kernel<Out, 4><<<blocks, kThreads, 0, stream>>>(
+                images, out, channels, height, width, patch, across, per_image, total);
+        } else {
+            extract_patches_kernel<Out, 1><<<blocks, kThreads, 0, stream>>>(
+                images, out, channels, height, width, patch, across, per_image, total);
+        }
+    };
     if (bf16) {
-        auto* out = static_cast<__nv_bfloat16*>(patches);
-        if (vec) {
-            extract_patches_kernel<__nv_bfloat16, 4><<<blocks, kThreads, 0, stream>>>(
-                images, out, channels, height, width, patch, across, per_image, total);
-        } else {
-            extract_patches_kernel<__nv_bfloat16, 1><<<blocks, kThreads, 0, stream>>>(
-                images, out, channels, height, width, patch, across, per_image, total);
-        }
+        run(static_cast<__nv_bfloat16*>(patches));
+    } else if (out_dtype == CUVIT_DTYPE_TF32) {
+        run(static_cast<Tf32*>(patches));
     } else {
-        auto* out = static_cast<float*>(patches);
-        if (vec) {
-            extract_patches_kernel<float, 4><<<blocks, kThreads, 0, stream>>>(
-                images, out, channels, height, width, patch, across, per_image, total);
-        } else {
-            extract_patches_kernel<float, 1><<<blocks, kThreads, 0, stream>>>(
-                images, out, channels, height, width, patch, across, per_image, total);
-        }
+        run(static_cast<float*>(patches));
     }
     return host::after_launch("extract_patches");
 }
@@ -694,6 +718,23 @@ int cuvit_convert_f32_to_bf16(const float* input, void* output, int64_t count,
                           reinterpret_cast<cudaStream_t>(stream)>>>(
         input, static_cast<__nv_bfloat16*>(output), count);
     return cuvit::host::after_launch("convert_f32_to_bf16");
+}
+
+int cuvit_round_to_tf32(const float* input, float* output, int64_t count,
+                        cuvit_stream_t stream) {
+    if (count == 0) {
+        return CUVIT_OK;
+    }
+    if (count < 0 || input == nullptr || output == nullptr) {
+        return fail(CUVIT_INVALID_ARGUMENT, "rounding arguments are invalid");
+    }
+    const long long grid = elementwise_grid(count);
+    if (grid < 0) {
+        return fail(CUVIT_LENGTH_ERROR, "Elementwise launch exceeds the CUDA grid limit");
+    }
+    round_tf32_kernel<<<static_cast<unsigned>(grid), kThreads, 0,
+                        reinterpret_cast<cudaStream_t>(stream)>>>(input, output, count);
+    return cuvit::host::after_launch("round_to_tf32");
 }
 
 } // extern "C"

@@ -32,7 +32,7 @@ __device__ __forceinline__ float load_operand(const T* pointer, long long index)
 template <typename T>
 __global__ void __launch_bounds__(kSimtThreads)
     simt_gemm_kernel(const T* __restrict__ a, const T* __restrict__ b,
-                     const float* __restrict__ bias, void* c, int c_bf16, int m, int n, int k,
+                     const float* __restrict__ bias, void* c, int c_kind, int m, int n, int k,
                      float alpha, int transposed, long long lda, long long ldb, long long ldc,
                      int count, int inner, long long stride_a, long long stride_b,
                      long long stride_c, long long outer_a, long long outer_b, long long outer_c,
@@ -129,13 +129,14 @@ __global__ void __launch_bounds__(kSimtThreads)
                     value = dev::gelu_erf(value);
                 }
                 const long long at = offset_c + row * ldc + col;
-                if (c_bf16) {
+                if (c_kind == 1) {
                     __nv_bfloat16* const out = static_cast<__nv_bfloat16*>(c);
                     out[at] = __float2bfloat16_rn(accumulate ? __bfloat162float(out[at]) + value
                                                              : value);
                 } else {
                     float* const out = static_cast<float*>(c);
-                    out[at] = accumulate ? out[at] + value : value;
+                    const float stored = accumulate ? out[at] + value : value;
+                    out[at] = c_kind == 2 ? dev::round_to_tf32(stored) : stored;
                 }
             }
         }
@@ -151,18 +152,18 @@ int launch_simt(const Resolved& r, cudaStream_t stream) {
     }
     const dim3 grid(static_cast<unsigned>(tiles_n), static_cast<unsigned>(tiles_m),
                     static_cast<unsigned>(p.batch.count < 65535 ? p.batch.count : 65535));
-    const int c_bf16 = r.c_dtype == CUVIT_DTYPE_BF16 ? 1 : 0;
+    const int c_kind = r.c_dtype;
     const cuvit_gemm_batch& batch = p.batch;
     if (r.math == CUVIT_MATH_BF16) {
         simt_gemm_kernel<__nv_bfloat16><<<grid, kSimtThreads, 0, stream>>>(
             static_cast<const __nv_bfloat16*>(r.a), static_cast<const __nv_bfloat16*>(r.b),
-            r.bias, r.c, c_bf16, p.m, p.n, p.k, p.alpha, r.transposed ? 1 : 0, r.lda, r.ldb,
+            r.bias, r.c, c_kind, p.m, p.n, p.k, p.alpha, r.transposed ? 1 : 0, r.lda, r.ldb,
             r.ldc, batch.count, batch.inner, batch.stride_a, batch.stride_b, batch.stride_c,
             batch.outer_stride_a, batch.outer_stride_b, batch.outer_stride_c,
             p.epilogue.accumulate ? 1 : 0, p.epilogue.gelu ? 1 : 0);
     } else {
         simt_gemm_kernel<float><<<grid, kSimtThreads, 0, stream>>>(
-            static_cast<const float*>(r.a), static_cast<const float*>(r.b), r.bias, r.c, c_bf16,
+            static_cast<const float*>(r.a), static_cast<const float*>(r.b), r.bias, r.c, c_kind,
             p.m, p.n, p.k, p.alpha, r.transposed ? 1 : 0, r.lda, r.ldb, r.ldc, batch.count,
             batch.inner, batch.stride_a, batch.stride_b, batch.stride_c, batch.outer_stride_a,
             batch.outer_stride_b, batch.outer_stride_c, p.epilogue.accumulate ? 1 : 0,
@@ -266,7 +267,7 @@ int resolve(const void* a, const void* b, const float* bias, void* c, int c_dtyp
     if (problem.layout != CUVIT_LAYOUT_NO_TRANSPOSE && problem.layout != CUVIT_LAYOUT_TRANSPOSED) {
         return host::fail(CUVIT_INVALID_ARGUMENT, "unknown GEMM layout");
     }
-    if (c_dtype != CUVIT_DTYPE_F32 && c_dtype != CUVIT_DTYPE_BF16) {
+    if (c_dtype != CUVIT_DTYPE_F32 && c_dtype != CUVIT_DTYPE_BF16 && c_dtype != CUVIT_DTYPE_TF32) {
         return host::fail(CUVIT_INVALID_ARGUMENT, "unknown output data type");
     }
     if (math != CUVIT_MATH_FP32 && math != CUVIT_MATH_TF32 && math != CUVIT_MATH_BF16) {
@@ -349,6 +350,9 @@ int prepare(const Resolved& r, Plan* plan) {
         tb.dims[1] = static_cast<uint64_t>(p.k);
         tb.box[0] = static_cast<uint32_t>(atom);
         tb.box[1] = static_cast<uint32_t>(block_k);
+        if (e == 4) {
+            tb.swizzle = CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B;
+        }
     }
     tb.strides_bytes[0] = static_cast<uint64_t>(r.ldb) * e;
     int b_index = 0, b_outer = 0;
@@ -394,8 +398,8 @@ int prepare(const Resolved& r, Plan* plan) {
     q.ldc = r.ldc;
     q.stride_c = p.batch.stride_c;
     q.outer_stride_c = p.batch.outer_stride_c;
-    q.c_bf16 = r.c_dtype == CUVIT_DTYPE_BF16 ? 1 : 0;
-    const int ce = q.c_bf16 ? 2 : 4;
+    q.c_kind = r.c_dtype;
+    const int ce = r.c_dtype == CUVIT_DTYPE_BF16 ? 2 : 4;
     const auto aligned16 = [ce](long long elements) { return (elements * ce) % 16 == 0; };
     q.c_vector_ok = (reinterpret_cast<uintptr_t>(r.c) % 16 == 0) && aligned16(r.ldc) &&
                             aligned16(p.batch.stride_c) && aligned16(p.batch.outer_stride_c)

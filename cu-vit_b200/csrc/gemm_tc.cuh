@@ -45,7 +45,7 @@ struct TcParams {
     const float* bias;
     void* c;
     long long ldc, stride_c, outer_stride_c;
-    int c_bf16;
+    int c_kind; // 0: FP32, 1: BF16, 2: FP32 storage rounded to TF32 values
     int c_vector_ok; // 16-byte vector stores of whole 32-column chunks are aligned
     int accumulate, gelu;
     unsigned* status;
@@ -61,7 +61,11 @@ struct TcShape {
     static constexpr int kStageBytes = (kABytes + kBBytes) * (Split ? 2 : 1);
     static constexpr int kStagesRaw = kSmemBudget / kStageBytes;
     static constexpr int kStages = kStagesRaw > 8 ? 8 : kStagesRaw;
-    static constexpr int kTmemColumns = 2 * BN < 32 ? 32 : 2 * BN;
+    // Per tile: one FP32 accumulator of BN columns, plus (Split) a second one that collects
+    // the small hi*lo and lo*hi cross terms, so the leading product's accumulator takes one
+    // rounding per MMA instead of three. Two tiles in flight.
+    static constexpr int kAccColumns = Split ? 2 * BN : BN;
+    static constexpr int kTmemColumns = 2 * kAccColumns < 32 ? 32 : 2 * kAccColumns;
     static constexpr int kThreads = Split ? 384 : 256;
     // barriers: full, empty, converted (split) per stage; tmem full/empty x2; drain
     static constexpr int kBarrierBytes = (3 * kStages + 5) * 8 + 16;
@@ -80,20 +84,6 @@ __device__ __forceinline__ void batch_coords(int entry, int inner, int& index, i
     }
 }
 
-// Rounds an FP32 value to the nearest TF32 (10-bit mantissa) value; non-finite values pass.
-__device__ __forceinline__ float round_to_tf32(float x) {
-    const uint32_t bits = __float_as_uint(x);
-    if ((bits & 0x7F800000u) == 0x7F800000u) {
-        return x;
-    }
-    const uint32_t rounded = (bits + 0x1000u) & 0xFFFFE000u;
-    // A carry into an all-ones exponent would turn a finite value into infinity.
-    if ((rounded & 0x7F800000u) == 0x7F800000u) {
-        return __uint_as_float(bits & 0xFFFFE000u);
-    }
-    return __uint_as_float(rounded);
-}
-
 template <int ElemBytes, int BN, bool BMnMajor, bool Split>
 __global__ void __launch_bounds__(TcShape<ElemBytes, BN, Split>::kThreads, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tma_a,
@@ -104,6 +94,11 @@ __global__ void __launch_bounds__(TcShape<ElemBytes, BN, Split>::kThreads, 1)
     constexpr uint32_t kFormat = ElemBytes == 2 ? 1u : 2u; // BF16 or TF32
     constexpr uint32_t kIdesc = dev::make_idesc(kFormat, kBlockM, BN, false, BMnMajor);
     constexpr uint32_t kTxBytes = Shape::kABytes + Shape::kBBytes;
+    // An MN-major B of 32-bit elements uses 32-byte swizzle atoms of 4 rows (512 bytes);
+    // 16-bit elements use the 8-row (1024-byte) atoms of the ordinary 128-byte swizzle.
+    constexpr uint32_t kBLayout =
+        ElemBytes == 4 ? dev::kLayoutSwizzle128Atom32 : dev::kLayoutSwizzle128;
+    constexpr uint32_t kBAtomBytes = ElemBytes == 4 ? 512u : 1024u;
 
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw_base = dev::smem_u32(smem_raw);
@@ -224,7 +219,8 @@ __global__ void __launch_bounds__(TcShape<ElemBytes, BN, Split>::kThreads, 1)
                 break;
             }
             dev::tc_fence_after();
-            const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+            const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * Shape::kAccColumns);
+            const uint32_t d_small = d_tmem + BN; // Split: the cross-term accumulator
             for (int kb = 0; kb < p.k_blocks; ++kb) {
                 const uint32_t ready = Split ? conv_bar(stage) : full_bar(stage);
                 if (!dev::mbar_wait(ready, phase, p.status)) {
@@ -242,8 +238,9 @@ __global__ void __launch_bounds__(TcShape<ElemBytes, BN, Split>::kThreads, 1)
                     if constexpr (!BMnMajor) {
                         b_desc = dev::smem_desc_sw128(b_addr + kk * 32, 16, 1024);
                     } else {
-                        b_desc = dev::smem_desc_sw128(b_addr + kk * Shape::kMmaK * kSwizzleBytes,
-                                                      Shape::kBlockK * kSwizzleBytes, 1024);
+                        b_desc = dev::smem_desc(b_addr + kk * Shape::kMmaK * kSwizzleBytes,
+                                                Shape::kBlockK * kSwizzleBytes, kBAtomBytes,
+                                                kBLayout);
                     }
                     const uint32_t accumulate = (kb > 0 || kk > 0) ? 1u : 0u;
                     if constexpr (Split) {
@@ -253,16 +250,15 @@ __global__ void __launch_bounds__(TcShape<ElemBytes, BN, Split>::kThreads, 1)
                             b_lo_desc =
                                 dev::smem_desc_sw128(b_addr + lo_offset + kk * 32, 16, 1024);
                         } else {
-                            b_lo_desc = dev::smem_desc_sw128(
+                            b_lo_desc = dev::smem_desc(
                                 b_addr + lo_offset + kk * Shape::kMmaK * kSwizzleBytes,
-                                Shape::kBlockK * kSwizzleBytes, 1024);
+                                Shape::kBlockK * kSwizzleBytes, kBAtomBytes, kBLayout);
                         }
                         const uint64_t a_lo_desc =
                             dev::smem_desc_sw128(a_addr + lo_offset + kk * 32, 16, 1024);
-                        // Small cross terms first, then the leading product.
-                        dev::mma_ss<kKind>(d_tmem, a_lo_desc, b_desc, kIdesc, accumulate);
-                        dev::mma_ss<kKind>(d_tmem, a_desc, b_lo_desc, kIdesc, 1u);
-                        dev::mma_ss<kKind>(d_tmem, a_desc, b_desc, kIdesc, 1u);
+                        dev::mma_ss<kKind>(d_small, a_lo_desc, b_desc, kIdesc, accumulate);
+                        dev::mma_ss<kKind>(d_small, a_desc, b_lo_desc, kIdesc, 1u);
+                        dev::mma_ss<kKind>(d_tmem, a_desc, b_desc, kIdesc, accumulate);
                     } else {
                         dev::mma_ss<kKind>(d_tmem, a_desc, b_desc, kIdesc, accumulate);
                     }
@@ -312,9 +308,21 @@ __global__ void __launch_bounds__(TcShape<ElemBytes, BN, Split>::kThreads, 1)
                 __syncwarp();
                 uint32_t raw[32];
                 const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
-                                       static_cast<uint32_t>(acc * BN + chunk * 32);
+                                       static_cast<uint32_t>(acc * Shape::kAccColumns +
+                                                             chunk * 32);
                 dev::tmem_load_32(taddr, raw);
-                dev::tmem_wait_load();
+                if constexpr (Split) {
+                    uint32_t small[32];
+                    dev::tmem_load_32(taddr + BN, small);
+                    dev::tmem_wait_load();
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        raw[j] = __float_as_uint(__uint_as_float(raw[j]) +
+                                                 __uint_as_float(small[j]));
+                    }
+                } else {
+                    dev::tmem_wait_load();
+                }
                 const int col0 = n_block * BN + chunk * 32;
                 if (row_ok && col0 < p.n) {
                 float v[32];
@@ -337,7 +345,7 @@ __global__ void __launch_bounds__(TcShape<ElemBytes, BN, Split>::kThreads, 1)
                     }
                 }
                 const bool whole = p.c_vector_ok && (col0 + 32 <= p.n);
-                if (!p.c_bf16) {
+                if (p.c_kind != 1) {
                     float* const out = static_cast<float*>(p.c) + row_offset + col0;
                     if (whole) {
                         float4* const out4 = reinterpret_cast<float4*>(out);
@@ -352,11 +360,18 @@ __global__ void __launch_bounds__(TcShape<ElemBytes, BN, Split>::kThreads, 1)
                                 value.z = old.z + value.z;
                                 value.w = old.w + value.w;
                             }
+                            if (p.c_kind == 2) {
+                                value.x = dev::round_to_tf32(value.x);
+                                value.y = dev::round_to_tf32(value.y);
+                                value.z = dev::round_to_tf32(value.z);
+                                value.w = dev::round_to_tf32(value.w);
+                            }
                             out4[q] = value;
                         }
                     } else {
                         for (int j = 0; j < 32 && col0 + j < p.n; ++j) {
-                            out[j] = p.accumulate ? out[j] + v[j] : v[j];
+                            const float value = p.accumulate ? out[j] + v[j] : v[j];
+                            out[j] = p.c_kind == 2 ? dev::round_to_tf32(value) : value;
                         }
                     }
                 } else {
@@ -421,15 +436,17 @@ __global__ void __launch_bounds__(TcShape<ElemBytes, BN, Split>::kThreads, 1)
             for (int i = t; i < kVectors; i += 128) {
                 const float4 x = hi[i];
                 float4 h;
-                h.x = round_to_tf32(x.x);
-                h.y = round_to_tf32(x.y);
-                h.z = round_to_tf32(x.z);
-                h.w = round_to_tf32(x.w);
+                h.x = dev::round_to_tf32(x.x);
+                h.y = dev::round_to_tf32(x.y);
+                h.z = dev::round_to_tf32(x.z);
+                h.w = dev::round_to_tf32(x.w);
+                // x - h is exact in FP32; rounding it (rather than letting the MMA truncate)
+                // leaves at most 2^-22 |x| of error per operand.
                 float4 l;
-                l.x = isfinite(x.x) ? x.x - h.x : 0.0F;
-                l.y = isfinite(x.y) ? x.y - h.y : 0.0F;
-                l.z = isfinite(x.z) ? x.z - h.z : 0.0F;
-                l.w = isfinite(x.w) ? x.w - h.w : 0.0F;
+                l.x = isfinite(x.x) ? dev::round_to_tf32(x.x - h.x) : 0.0F;
+                l.y = isfinite(x.y) ? dev::round_to_tf32(x.y - h.y) : 0.0F;
+                l.z = isfinite(x.z) ? dev::round_to_tf32(x.z - h.z) : 0.0F;
+                l.w = isfinite(x.w) ? dev::round_to_tf32(x.w - h.w) : 0.0F;
                 hi[i] = h;
                 lo[i] = l;
             }

@@ -163,17 +163,26 @@ __device__ __forceinline__ void tc_commit(uint32_t bar) {
         : "memory");
 }
 
+// Shared-memory layouts a matrix descriptor can name (bits 61..63).
+constexpr uint32_t kLayoutSwizzle128 = 2;       // 16-byte chunks over 128-byte rows, 8-row atoms
+constexpr uint32_t kLayoutSwizzle128Atom32 = 1; // 32-byte chunks over 128-byte rows, 4-row atoms
+
 // Shared-memory matrix descriptor (tcgen05 "matrix descriptor"): start address, leading and
-// stride byte offsets (16-byte units), descriptor version 1, 128-byte swizzle.
-__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t address, uint32_t lbo_bytes,
-                                                    uint32_t sbo_bytes) {
+// stride byte offsets (16-byte units), descriptor version 1, swizzle layout.
+__device__ __forceinline__ uint64_t smem_desc(uint32_t address, uint32_t lbo_bytes,
+                                              uint32_t sbo_bytes, uint32_t layout) {
     uint64_t desc = 0;
     desc |= static_cast<uint64_t>((address & 0x3FFFFu) >> 4);
     desc |= static_cast<uint64_t>((lbo_bytes >> 4) & 0x3FFFu) << 16;
     desc |= static_cast<uint64_t>((sbo_bytes >> 4) & 0x3FFFu) << 32;
     desc |= 1ull << 46;
-    desc |= 2ull << 61;
+    desc |= static_cast<uint64_t>(layout) << 61;
     return desc;
+}
+
+__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t address, uint32_t lbo_bytes,
+                                                    uint32_t sbo_bytes) {
+    return smem_desc(address, lbo_bytes, sbo_bytes, kLayoutSwizzle128);
 }
 
 // Instruction descriptor for kind::f16 / kind::tf32 with FP32 accumulation.
@@ -278,6 +287,22 @@ __device__ __forceinline__ void tmem_wait_store() {
 // (src/kernels/gemm.cu:157-160).
 __device__ __forceinline__ float gelu_erf(float value) {
     return 0.5F * value * (1.0F + erff(value * 0.7071067811865475F));
+}
+
+// Rounds an FP32 value to the nearest TF32 value (10-bit mantissa, ties away from zero in
+// magnitude); non-finite values pass through. The tensor core would otherwise truncate the
+// low 13 mantissa bits of a TF32 operand, a bias that accumulates over long reductions.
+__device__ __forceinline__ float round_to_tf32(float x) {
+    const uint32_t bits = __float_as_uint(x);
+    if ((bits & 0x7F800000u) == 0x7F800000u) {
+        return x;
+    }
+    const uint32_t rounded = (bits + 0x1000u) & 0xFFFFE000u;
+    // A carry into an all-ones exponent would turn a finite value into infinity.
+    if ((rounded & 0x7F800000u) == 0x7F800000u) {
+        return __uint_as_float(bits & 0xFFFFE000u);
+    }
+    return __uint_as_float(rounded);
 }
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float low, float high) {

@@ -161,7 +161,7 @@ int encode_tma(const TmaTensor& tensor, CUtensorMap* map) {
     const CUresult result =
         encode(map, tensor.type, static_cast<cuuint32_t>(tensor.rank),
                const_cast<void*>(tensor.base), dims, strides, box, element_strides,
-               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, tensor.swizzle,
                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (result != CUDA_SUCCESS) {
         return fail(CUVIT_CUDA_ERROR,

@@ -72,6 +72,9 @@ struct TmaTensor {
     uint64_t dims[4] = {1, 1, 1, 1};
     uint64_t strides_bytes[3] = {0, 0, 0};
     uint32_t box[4] = {1, 1, 1, 1};
+    // 16-byte chunks swizzled over 128-byte rows, or 32-byte chunks (the only smem layout
+    // the tensor core accepts for MN-major 32-bit operands).
+    CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B;
 };
 
 // Whether TMA can describe the tensor: 16-byte aligned base, strides multiples of 16 bytes

@@ -165,8 +165,18 @@ struct cuvit_vit {
 namespace cuvit::model {
 namespace {
 
+// Storage of the activations a GEMM or the attention consumes next: bfloat16, TF32-rounded
+// floats (so the TF32 tensor core sees round-to-nearest operands, not truncated ones), or
+// full floats for the FP32-faithful path.
 int compute_dtype(const cuvit_vit& m) {
-    return m.precision == CUVIT_MATH_BF16 ? CUVIT_DTYPE_BF16 : CUVIT_DTYPE_F32;
+    switch (m.precision) {
+    case CUVIT_MATH_BF16:
+        return CUVIT_DTYPE_BF16;
+    case CUVIT_MATH_TF32:
+        return CUVIT_DTYPE_TF32;
+    default:
+        return CUVIT_DTYPE_F32;
+    }
 }
 
 int element_bytes(const cuvit_vit& m) { return m.precision == CUVIT_MATH_BF16 ? 2 : 4; }
@@ -456,6 +466,15 @@ int build(cuvit_vit* m, const float* const* host) {
             status = host::check_cuda(
                 cudaMemcpy(target, host[i], count * sizeof(float), cudaMemcpyHostToDevice),
                 "cudaMemcpy(weights)");
+            if (status == CUVIT_OK && spec.gemm_weight && m->precision == CUVIT_MATH_TF32) {
+                // TF32 operands are rounded to nearest once here; the tensor core would
+                // otherwise truncate them on every use.
+                float* const values = static_cast<float*>(target);
+                status = cuvit_round_to_tf32(values, values, count, nullptr);
+                if (status == CUVIT_OK) {
+                    status = host::check_cuda(cudaDeviceSynchronize(), "cudaDeviceSynchronize");
+                }
+            }
         }
     }
     if (staging != nullptr) {

@@ -25,6 +25,7 @@ LAYOUT_NO_TRANSPOSE = 0
 LAYOUT_TRANSPOSED = 1
 DTYPE_F32 = 0
 DTYPE_BF16 = 1
+DTYPE_TF32 = 2
 MATH_FP32 = 0
 MATH_TF32 = 1
 MATH_BF16 = 2
@@ -117,6 +118,7 @@ SIGNATURES = {
     "cuvit_broadcast": (_i, [_vp, _vp, _i64, _i64, _i, _vp]),
     "cuvit_init_tokens": (_i, [_vp, _vp, _vp, _i, _i, _i, _vp]),
     "cuvit_convert_f32_to_bf16": (_i, [_vp, _vp, _i64, _vp]),
+    "cuvit_round_to_tf32": (_i, [_vp, _vp, _i64, _vp]),
     "cuvit_attention": (_i, [_vp, _vp, _i, _i, _i, _i, _i, _f, _vp]),
     "cuvit_device_status": (_i, [ctypes.POINTER(ctypes.c_uint)]),
     "cuvit_launch_count": (ctypes.c_longlong, []),

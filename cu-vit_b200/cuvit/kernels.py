@@ -20,6 +20,7 @@ LAYOUT_NO_TRANSPOSE = _lib.LAYOUT_NO_TRANSPOSE
 LAYOUT_TRANSPOSED = _lib.LAYOUT_TRANSPOSED
 DTYPE_F32 = _lib.DTYPE_F32
 DTYPE_BF16 = _lib.DTYPE_BF16
+DTYPE_TF32 = _lib.DTYPE_TF32
 MATH_FP32 = _lib.MATH_FP32
 MATH_TF32 = _lib.MATH_TF32
 MATH_BF16 = _lib.MATH_BF16
@@ -190,6 +191,11 @@ def launch_init_tokens(tokens, class_token, position, batch: int, tokens_per_ima
 def launch_convert_f32_to_bf16(input, output, count: int, stream=None) -> None:
     check(_lib.library().cuvit_convert_f32_to_bf16(_ptr(input), _ptr(output), count,
                                                    _stream(stream)))
+
+
+def launch_round_to_tf32(input, output, count: int, stream=None) -> None:
+    check(_lib.library().cuvit_round_to_tf32(_ptr(input), _ptr(output), count,
+                                             _stream(stream)))
 
 
 def launch_attention(qkv, context, dtype: int, batch: int, tokens: int, heads: int,

@@ -8,7 +8,7 @@ import dataclasses
 import numpy as np
 
 from . import _lib
-from .errors import check
+from .errors import InvalidArgument, check
 from .kernels import _ptr, _stream
 
 PRECISION_FP32 = _lib.MATH_FP32
@@ -191,12 +191,14 @@ class VisionTransformer:
         per_image = self.image_elements()
         flat = np.ascontiguousarray(images, dtype=np.float32).reshape(-1)
         if per_image == 0 or flat.size % per_image != 0:
-            raise ValueError(f"The input holds {flat.size} elements, which is not a whole "
-                             f"number of {per_image}-element images")
+            raise InvalidArgument(_lib.INVALID_ARGUMENT,
+                                  f"The input holds {flat.size} elements, which is not a whole "
+                                  f"number of {per_image}-element images")
         batch = flat.size // per_image
         if batch > self.max_batch:
-            raise ValueError(f"This model was built for at most {self.max_batch} images, but "
-                             f"{batch} were given")
+            raise InvalidArgument(_lib.INVALID_ARGUMENT,
+                                  f"This model was built for at most {self.max_batch} images, "
+                                  f"but {batch} were given")
         logits = np.empty((batch, self.config.classes), np.float32)
         check(_lib.library().cuvit_vit_forward_host(self._handle, flat.ctypes.data,
                                                     logits.ctypes.data, batch, _stream(stream)))

@@ -108,7 +108,15 @@ typedef struct cuvit_gemm_problem {
  * one un-batched problem, packed operands, alpha 1, no epilogue. */
 void cuvit_gemm_problem_init(cuvit_gemm_problem* problem, int m, int n, int k, int layout);
 
-typedef enum cuvit_dtype { CUVIT_DTYPE_F32 = 0, CUVIT_DTYPE_BF16 = 1 } cuvit_dtype;
+/* Storage types. TF32 is float storage holding values rounded to the nearest TF32 value
+ * (10-bit mantissa): what a producer writes for a tensor that a TF32 tensor-core operation
+ * consumes next, which would otherwise truncate the low mantissa bits (a bias that
+ * accumulates over long reductions). */
+typedef enum cuvit_dtype {
+    CUVIT_DTYPE_F32 = 0,
+    CUVIT_DTYPE_BF16 = 1,
+    CUVIT_DTYPE_TF32 = 2
+} cuvit_dtype;
 
 /* Arithmetic of a float GEMM.
  *   FP32: FP32-faithful. Tensor-core 3xTF32 split (hi*hi + hi*lo + lo*hi with FP32
@@ -128,7 +136,7 @@ int cuvit_set_math_mode(int math);
 int cuvit_get_math_mode(void);
 
 /* Typed GEMM: a/b are bfloat16 when math is CUVIT_MATH_BF16 and float otherwise; c is
- * c_dtype (CUVIT_DTYPE_F32 or CUVIT_DTYPE_BF16, accumulate reads it in that type); bias is
+ * c_dtype (F32, BF16, or TF32-rounded float; accumulate reads it in that type); bias is
  * float. Same problem semantics as cuvit_gemm(). */
 int cuvit_gemm_ex(const void* a, const void* b, const float* bias, void* c, int c_dtype,
                   int math, const cuvit_gemm_problem* problem, cuvit_stream_t stream);
@@ -194,14 +202,20 @@ int cuvit_init_tokens(float* tokens, const float* class_token, const float* posi
 int cuvit_convert_f32_to_bf16(const float* input, void* output, int64_t count,
                               cuvit_stream_t stream);
 
+/* Rounds count floats to the nearest TF32 value, kept in float storage (CUVIT_DTYPE_TF32);
+ * input may equal output. */
+int cuvit_round_to_tf32(const float* input, float* output, int64_t count,
+                        cuvit_stream_t stream);
+
 /* ---------------------------------------------------------------------------------------
  * Fused attention. Replaces the Q.K^T GEMM -> launch_softmax -> .V GEMM sequence of
  * src/model/vit.cu:198-242 with one kernel that keeps the T x T logits on chip.
  *
  * qkv:     [batch * tokens, 3 * heads * head_dim], each row packed [3][heads][head_dim]
  * context: [batch * tokens, heads * head_dim], head h in columns h*head_dim ..
- * dtype:   CUVIT_DTYPE_BF16 (BF16 tensor cores) or CUVIT_DTYPE_F32 (TF32 tensor cores);
- *          qkv and context share it. Softmax statistics are FP32.
+ * dtype:   CUVIT_DTYPE_BF16 (BF16 tensor cores), CUVIT_DTYPE_F32 (float storage, TF32
+ *          tensor cores) or CUVIT_DTYPE_TF32 (the same, context stored rounded to TF32
+ *          values); qkv and context share the storage type. Softmax statistics are FP32.
  * Supported: head_dim == 64, 1 <= tokens <= 256, 16-byte aligned rows.
  * ------------------------------------------------------------------------------------- */
 int cuvit_attention(const void* qkv, void* context, int dtype, int batch, int tokens,

@@ -114,7 +114,7 @@ def test_attention_validation():
         kernels.launch_attention(FAKE, FAKE, kernels.DTYPE_BF16, 1, 300, 12, 64, 0.125)
     with pytest.raises(InvalidArgument, match="aligned"):
         kernels.launch_attention(FAKE + 4, FAKE, kernels.DTYPE_BF16, 1, 197, 12, 64, 0.125)
-    with pytest.raises(InvalidArgument, match="BF16 or F32"):
+    with pytest.raises(InvalidArgument, match="BF16, F32 or TF32"):
         kernels.launch_attention(FAKE, FAKE, 9, 1, 197, 12, 64, 0.125)
 
 

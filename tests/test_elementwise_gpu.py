@@ -169,6 +169,39 @@ def test_conversion_rounds_to_nearest_even(cuda):
     np.testing.assert_array_equal(to_host(out), bf16_round(x))
 
 
+def tf32_round(x):
+    """Round to nearest TF32 value (ties away from zero in magnitude), float32 storage."""
+    bits = np.ascontiguousarray(x, np.float32).view(np.uint32).astype(np.uint64)
+    rounded = ((bits + 0x1000) & 0xFFFFE000).astype(np.uint32)
+    return rounded.view(np.float32)
+
+
+def test_tf32_storage_outputs(cuda):
+    """CUVIT_DTYPE_TF32: float storage holding round-to-nearest TF32 values."""
+    rng = np.random.default_rng(23)
+    x = rng.standard_normal(4097).astype(np.float32)
+    out = to_device(np.zeros_like(x))
+    kernels.launch_round_to_tf32(to_device(x), out, x.size)
+    np.testing.assert_array_equal(to_host(out), tf32_round(x))
+    rows, columns = 9, 192
+    x = rng.standard_normal(rows * columns).astype(np.float32)
+    g = np.ones(columns, np.float32)
+    b = np.zeros(columns, np.float32)
+    full = to_device(np.zeros(rows * columns))
+    rounded = to_device(np.zeros(rows * columns))
+    kernels.launch_layer_norm_ex(to_device(x), 0, to_device(g), to_device(b), full,
+                                 kernels.DTYPE_F32, 0, rows, columns)
+    kernels.launch_layer_norm_ex(to_device(x), 0, to_device(g), to_device(b), rounded,
+                                 kernels.DTYPE_TF32, 0, rows, columns)
+    np.testing.assert_array_equal(to_host(rounded), tf32_round(to_host(full)))
+    images = rng.standard_normal(2 * 3 * 32 * 32).astype(np.float32)
+    patches = to_device(np.zeros(images.size))
+    kernels.launch_extract_patches_ex(to_device(images), patches, kernels.DTYPE_TF32, 2, 3, 32,
+                                      32, 8)
+    np.testing.assert_array_equal(to_host(patches),
+                                  tf32_round(oracle.extract_patches(images, 2, 3, 32, 32, 8)))
+
+
 def test_invalid_arguments_on_device_buffers(cuda):
     buffer = to_device(np.zeros(16))
     kernels.launch_gelu(buffer, buffer, 0)
