@@ -208,6 +208,7 @@ def our_arm(args) -> None:
     import torch.distributed as dist
 
     import cuvit
+    from cuvit.replicas import gather_logits
     from cuvit.vit import (PRECISION_BF16, PRECISION_TF32, VisionTransformer, VitConfig,
                            random_weights)
 
@@ -230,14 +231,11 @@ def our_arm(args) -> None:
     host_images = rng.standard_normal(batch * config.image_elements()).astype(np.float32)
     images = torch.from_numpy(host_images).to(device)
     logits = torch.zeros(batch, config.classes, device=device)
-    gathered = ([torch.zeros_like(logits) for _ in range(world)]
-                if (world > 1 and rank == 0) else None)
     stream = torch.cuda.current_stream(device)
 
     def step():
         model.forward_graph(images, logits, batch, stream)
-        if world > 1:
-            dist.gather(logits, gathered, dst=0)
+        gather_logits(logits, world, rank)  # the path's only collective (N > 1)
 
     def barrier():
         if world > 1:
@@ -301,10 +299,7 @@ def our_arm(args) -> None:
     gemm_launches = sum(e["launches"] for e in gemm)
     achieved_tflops = gemm_flops / (gemm_ms * 1e-3) / 1e12
     peak, peak_kind = peaks()
-    traffic = None
-    traffic_file = ROOT / "profiles" / "traffic.json"
-    if traffic_file.exists():
-        traffic = json.loads(traffic_file.read_text()).get(f"{args.config}/gemm")
+    traffic, traffic_launch = gemm_traffic(args.config, label, batch, precision_name)
 
     # End to end through the public host-buffer API: pinned host images in, logits out.
     pinned_images = torch.from_numpy(host_images).pin_memory()
@@ -316,7 +311,7 @@ def our_arm(args) -> None:
                                stream)
         if world > 1:
             device_logits.copy_(pinned_logits, non_blocking=False)
-            dist.gather(device_logits, gathered, dst=0)
+            gather_logits(device_logits, world, rank)
 
     for _ in range(args.warmup):
         e2e_step()
@@ -367,6 +362,7 @@ def our_arm(args) -> None:
                 "frac_of_burst": achieved_tflops / burst,
                 "frac_of_nominal_2250": achieved_tflops / 2250.0,
                 "traffic": traffic,
+                "traffic_launch": traffic_launch,
                 "launches_per_pass": gemm_launches // passes,
                 "flops_per_launch": gemm_flops / max(gemm_launches, 1),
             },
@@ -379,6 +375,20 @@ def our_arm(args) -> None:
     model.close()
     if world > 1:
         dist.destroy_process_group()
+
+
+def gemm_traffic(config_name: str, label: str, batch: int, precision: str):
+    """DRAM bytes (read + write) of one GEMM launch from the committed ncu summary, if any:
+    profiles/tc_gemm_fc1_<config>_b<batch>_<precision>.md, line 'traffic_bytes_per_launch'."""
+    import re
+
+    path = ROOT / "profiles" / f"tc_gemm_fc1_{config_name}_b{batch}_{precision}.md"
+    if not path.exists():
+        return None, None
+    match = re.search(r"^traffic_bytes_per_launch:\s*(\d+)", path.read_text(), re.M)
+    if not match:
+        return None, None
+    return int(match.group(1)), f"{label} block-0 FC1 GEMM, one ncu capture ({path.name})"
 
 
 def measure_cpu_baseline(config, weights, seed) -> dict | None:

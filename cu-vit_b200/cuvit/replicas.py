@@ -1,0 +1,47 @@
+"""Data-parallel replicas: one process per GPU, the batch sharded by image, weights
+replicated, and the logits gathered to rank 0 -- the only collective of the path (images never
+interact, so nothing is exchanged per layer).
+
+The helpers work on any torch.distributed backend (NCCL on GPUs, gloo on CPU for tests).
+"""
+
+from __future__ import annotations
+
+
+def shard(total: int, world: int, rank: int) -> tuple[int, int]:
+    """Contiguous slice [start, start + count) of `total` images owned by `rank`; the first
+    total % world ranks take one extra image. Global image b lives on the rank whose slice
+    contains b, so gathering in rank order restores the global order."""
+    if world < 1 or not 0 <= rank < world:
+        raise ValueError(f"rank {rank} outside a world of {world}")
+    if total < 0:
+        raise ValueError("total cannot be negative")
+    base, extra = divmod(total, world)
+    start = rank * base + min(rank, extra)
+    return start, base + (1 if rank < extra else 0)
+
+
+def gather_logits(local, world: int, rank: int, counts: list[int] | None = None):
+    """Gathers every rank's [count, classes] logits to rank 0 in rank order.
+
+    counts: per-rank row counts (defaults to equal shards). Returns the concatenated tensor
+    on rank 0 and None elsewhere. Every rank must call it, in the same order as its other
+    collectives.
+    """
+    import torch
+    import torch.distributed as dist
+
+    if world == 1:
+        return local
+    counts = counts or [local.shape[0]] * world
+    rows = max(counts)
+    padded = local
+    if local.shape[0] < rows:  # gather needs equal shapes
+        padded = torch.zeros((rows,) + tuple(local.shape[1:]), dtype=local.dtype,
+                             device=local.device)
+        padded[: local.shape[0]] = local
+    buffers = [torch.empty_like(padded) for _ in range(world)] if rank == 0 else None
+    dist.gather(padded, buffers, dst=0)
+    if rank != 0:
+        return None
+    return torch.cat([buffers[r][: counts[r]] for r in range(world)])

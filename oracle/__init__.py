@@ -31,7 +31,7 @@ _f = ctypes.c_float
 
 def build(reference: bool = False) -> None:
     """Builds liboracle.so (and the _ref libraries when reference=True)."""
-    targets = ["oracle"] + (["ref"] if reference else [])
+    targets = ["oracle"] + (["ref", "ref-tests"] if reference else [])
     subprocess.run(["make", "-s", "-C", str(HERE), *targets], check=True)
 
 

@@ -1,0 +1,114 @@
+"""Multi-rank host logic on the CPU with gloo (world size 2 and 3): batch sharding, the
+logits gather in global image order, and a rank that fails before the collective.
+
+The per-rank "forward pass" is the CPU oracle on a tiny ViT, so the gathered logits can be
+checked against one whole-batch oracle run; on GPUs the same helpers run over NCCL with the
+CUDA library computing each shard (bench.py).
+"""
+
+from __future__ import annotations
+
+import datetime
+import os
+import pathlib
+import socket
+import sys
+import traceback
+
+import numpy as np
+import pytest
+import torch.multiprocessing as mp
+
+ROOT = pathlib.Path(__file__).resolve().parents[1]
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, total, mode, results):
+    sys.path.insert(0, str(ROOT))
+    sys.path.insert(0, str(ROOT / "cu-vit_b200"))
+    try:
+        import torch
+        import torch.distributed as dist
+
+        import oracle
+        from cuvit.replicas import gather_logits, shard
+        from cuvit.vit import VitConfig, random_weights, tensor_specs
+
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        dist.init_process_group("gloo", rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=20))
+        config = VitConfig(16, 4, 3, 16, 2, 2, 32, 5)
+        weights = random_weights(config, 9, std=0.3)
+        images = np.random.default_rng(4).standard_normal(
+            total * config.image_elements()).astype(np.float32)
+        start, count = shard(total, world, rank)
+        per_image = config.image_elements()
+        mine = images[start * per_image:(start + count) * per_image]
+        if mode == "fail" and rank == 1:
+            raise RuntimeError("rank 1 failed before the gather")
+        logits = torch.from_numpy(
+            oracle.vit_forward(config, weights, tensor_specs(config), mine, threads=1))
+        counts = [shard(total, world, r)[1] for r in range(world)]
+        gathered = gather_logits(logits, world, rank, counts)
+        if rank == 0:
+            want = oracle.vit_forward(config, weights, tensor_specs(config), images, threads=2)
+            results[rank] = ("ok", bool(np.array_equal(gathered.numpy(), want)))
+        else:
+            results[rank] = ("ok", gathered is None)
+        dist.destroy_process_group()
+    except Exception as error:  # reported to the parent, which decides pass/fail
+        results[rank] = ("error", f"{type(error).__name__}: {error}\n{traceback.format_exc()}")
+
+
+def _run(world, total, mode):
+    ctx = mp.get_context("spawn")
+    with ctx.Manager() as manager:
+        results = manager.dict()
+        port = _free_port()
+        procs = [ctx.Process(target=_worker, args=(r, world, port, total, mode, results))
+                 for r in range(world)]
+        for p in procs:
+            p.start()
+        for p in procs:
+            p.join(timeout=120)
+            if p.is_alive():
+                p.kill()
+        return dict(results)
+
+
+def test_shard_covers_the_batch_in_order():
+    from cuvit.replicas import shard
+
+    for total in (0, 1, 7, 256, 1024, 1027):
+        for world in (1, 2, 3, 8):
+            spans = [shard(total, world, r) for r in range(world)]
+            assert spans[0][0] == 0
+            for (s0, c0), (s1, _) in zip(spans, spans[1:]):
+                assert s0 + c0 == s1
+            assert sum(c for _, c in spans) == total
+            assert max(c for _, c in spans) - min(c for _, c in spans) <= 1
+    with pytest.raises(ValueError):
+        shard(8, 2, 2)
+
+
+@pytest.mark.parametrize("world,total", [(2, 6), (3, 7)])
+def test_gathered_logits_equal_one_whole_batch(world, total):
+    results = _run(world, total, "ok")
+    assert len(results) == world, results
+    for rank, (status, value) in sorted(results.items()):
+        assert status == "ok", value
+        assert value is True, f"rank {rank}"
+
+
+def test_a_failed_rank_surfaces_as_an_error_not_a_hang():
+    results = _run(2, 4, "fail")
+    assert results.get(1, ("", ""))[0] == "error"
+    # rank 0 either errors out of the gather (peer gone / timeout) -- it must not report ok
+    status, _ = results.get(0, ("missing", ""))
+    assert status in ("error", "missing")
