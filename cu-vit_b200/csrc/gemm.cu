@@ -408,6 +408,40 @@ int prepare(const Resolved& r, Plan* plan) {
     q.accumulate = p.epilogue.accumulate ? 1 : 0;
     q.gelu = p.epilogue.gelu ? 1 : 0;
     q.status = context->status;
+    q.bias_vector_ok =
+        r.bias != nullptr && reinterpret_cast<uintptr_t>(r.bias) % 16 == 0 ? 1 : 0;
+
+    // C through TMA when a descriptor can describe it: 128-byte rows of 32 FP32 or 64 BF16
+    // columns, 32 rows per warp. Accumulating into FP32 becomes a TMA reduce-add (one FP32
+    // add in L2, the same single rounding as read-add-write); accumulating into BF16 or
+    // TF32 storage has to round in that type, so it keeps the direct path.
+    q.c_tma = 0;
+    const bool reduce_ok = !p.epilogue.accumulate || r.c_dtype == CUVIT_DTYPE_F32;
+    const bool chunk_ok = r.c_dtype != CUVIT_DTYPE_BF16 || bn >= 128;
+    if (reduce_ok && chunk_ok) {
+        host::TmaTensor tc;
+        tc.base = r.c;
+        tc.type = r.c_dtype == CUVIT_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+        tc.element_bytes = ce;
+        tc.rank = 2;
+        tc.dims[0] = static_cast<uint64_t>(p.n);
+        tc.dims[1] = static_cast<uint64_t>(p.m);
+        tc.strides_bytes[0] = static_cast<uint64_t>(r.ldc) * ce;
+        tc.box[0] = static_cast<uint32_t>(kSwizzleBytes / ce);
+        tc.box[1] = 32;
+        int c_index = 0, c_outer = 0;
+        if (add_batch_dims(p.batch, p.batch.stride_c, p.batch.outer_stride_c, ce, &tc, &c_index,
+                           &c_outer) &&
+            host::tma_describable(tc) && host::encode_tma(tc, &plan->map_c) == CUVIT_OK) {
+            q.c_tma = 1;
+            q.c_rank = tc.rank;
+            q.c_has_index = c_index;
+            q.c_has_outer = c_outer;
+        } else {
+            host::clear_error();
+        }
+    }
 
     plan->elem_bytes = e;
     plan->block_n = bn;

@@ -32,6 +32,7 @@ struct Plan {
     // tensor-core path
     CUtensorMap map_a{};
     CUtensorMap map_b{};
+    CUtensorMap map_c{}; // output, for TMA stores / reduce-adds (params.c_tma)
     TcParams params{};
     int elem_bytes = 4;
     int block_n = 128;

@@ -5,17 +5,20 @@
 // A is row-major [M, K] (K-major). B is either [N, K] (K-major, the reference's
 // kTransposed layout) or [K, N] (MN-major, kNoTranspose). Operands arrive by TMA with
 // 128-byte swizzle into a ring of shared-memory stages; one thread issues tcgen05.mma into
-// a double-buffered FP32 accumulator in tensor memory; four epilogue warps drain TMEM,
-// apply alpha / bias / GELU / accumulate and store C while the next tile accumulates.
+// a double-buffered FP32 accumulator in tensor memory; eight epilogue warps drain TMEM,
+// apply alpha / bias / GELU, and write C through shared memory with TMA stores -- or TMA
+// reduce-adds, which make "accumulate into the residual stream" an FP32 add in L2 without
+// the epilogue ever reading C -- while the next tile accumulates.
 //
 // Roles (one CTA per SM, persistent over output tiles 128 x BN):
-//   warp 0        TMA producer (one elected lane)
-//   warp 1        MMA issuer (one elected lane)
-//   warp 2        TMEM allocator
-//   warps 4..7    epilogue, warp w owns TMEM lanes 32*(w%4) .. +31 (= tile rows)
-//   warps 8..11   (Split only) 3xTF32 splitter: rewrites each landed stage as
-//                 hi = tf32(x) in place and lo = x - hi beside it, so the MMA warp can
-//                 issue hi*hi + hi*lo + lo*hi.
+//   warp 0         TMA producer (one elected lane)
+//   warp 1         MMA issuer (one elected lane)
+//   warp 2         TMEM allocator
+//   warps 4..11    epilogue: warp w reads TMEM lanes 32*(w%4) .. +31 (= tile rows) and
+//                  column half (w-4)/4 of the tile
+//   warps 12..15   (Split only) 3xTF32 splitter: rewrites each landed stage as
+//                  hi = rn_tf32(x) in place and lo = rn_tf32(x - hi) beside it, so the MMA
+//                  warp can issue hi*hi + hi*lo + lo*hi.
 //
 // Numerics: each output element's K reduction runs in a fixed order that depends only on
 // K (no split-K), so results do not depend on M, the batch, or the tile chosen for M.
@@ -31,32 +34,37 @@
 namespace cuvit::gemm {
 
 constexpr int kBlockM = 128;
-constexpr int kSwizzleBytes = 128; // one swizzle atom row
+constexpr int kSwizzleBytes = 128;  // one swizzle atom row
 constexpr int kSmemBudget = 196608; // operand stages per CTA
+constexpr int kEpilogueWarps = 8;
+constexpr int kEpilogueThreads = 32 * kEpilogueWarps;
+constexpr int kSlabBytes = 32 * kSwizzleBytes; // one warp's 32 output rows x 128 bytes
 
 struct TcParams {
     int m, n, k;
     int m_tiles, n_tiles, k_blocks;
     int total_tiles;
     int count, inner; // batch entries; inner > 0 splits entry e into (e / inner, e % inner)
-    int a_rank, b_rank;
-    int a_has_index, a_has_outer, b_has_index, b_has_outer;
+    int a_rank, b_rank, c_rank;
+    int a_has_index, a_has_outer, b_has_index, b_has_outer, c_has_index, c_has_outer;
     float alpha;
     const float* bias;
+    int bias_vector_ok; // bias is 16-byte aligned
     void* c;
     long long ldc, stride_c, outer_stride_c;
-    int c_kind; // 0: FP32, 1: BF16, 2: FP32 storage rounded to TF32 values
-    int c_vector_ok; // 16-byte vector stores of whole 32-column chunks are aligned
+    int c_kind;      // 0: FP32, 1: BF16, 2: FP32 storage rounded to TF32 values
+    int c_tma;       // write C with TMA stores (reduce-adds when accumulating)
+    int c_vector_ok; // direct path: 16-byte vector stores of whole chunks are aligned
     int accumulate, gelu;
     unsigned* status;
 };
 
 template <int ElemBytes, int BN, bool Split>
 struct TcShape {
-    static constexpr int kBlockK = kSwizzleBytes / ElemBytes;       // K elements per stage
-    static constexpr int kMmaK = 32 / ElemBytes;                     // K per instruction
-    static constexpr int kAtomElems = kSwizzleBytes / ElemBytes;     // MN elements per atom
-    static constexpr int kABytes = kBlockM * kSwizzleBytes;          // 16 KiB
+    static constexpr int kBlockK = kSwizzleBytes / ElemBytes;   // K elements per stage
+    static constexpr int kMmaK = 32 / ElemBytes;                 // K per instruction
+    static constexpr int kAtomElems = kSwizzleBytes / ElemBytes; // MN elements per atom
+    static constexpr int kABytes = kBlockM * kSwizzleBytes;      // 16 KiB
     static constexpr int kBBytes = BN * kSwizzleBytes;
     static constexpr int kStageBytes = (kABytes + kBBytes) * (Split ? 2 : 1);
     static constexpr int kStagesRaw = kSmemBudget / kStageBytes;
@@ -66,12 +74,15 @@ struct TcShape {
     // rounding per MMA instead of three. Two tiles in flight.
     static constexpr int kAccColumns = Split ? 2 * BN : BN;
     static constexpr int kTmemColumns = 2 * kAccColumns < 32 ? 32 : 2 * kAccColumns;
-    static constexpr int kThreads = Split ? 384 : 256;
+    static constexpr int kThreads = 32 * (4 + kEpilogueWarps + (Split ? 4 : 0));
+    static constexpr int kSlabOffset = kStages * kStageBytes;
+    static constexpr int kBarrierOffset = kSlabOffset + kEpilogueWarps * kSlabBytes;
     // barriers: full, empty, converted (split) per stage; tmem full/empty x2; drain
     static constexpr int kBarrierBytes = (3 * kStages + 5) * 8 + 16;
-    static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kBarrierBytes;
+    static constexpr int kSmemBytes = 1024 + kBarrierOffset + kBarrierBytes;
     static_assert(kStages >= 2, "at least two pipeline stages");
-    static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "BN must be 32..256, multiple of 32");
+    static_assert(BN % 64 == 0 && BN >= 64 && BN <= 256, "BN must be 64, 128 or 256");
+    static_assert(kSmemBytes <= 232448, "shared memory over the per-block limit");
 };
 
 __device__ __forceinline__ void batch_coords(int entry, int inner, int& index, int& outer) {
@@ -84,10 +95,210 @@ __device__ __forceinline__ void batch_coords(int entry, int inner, int& index, i
     }
 }
 
+// Loads Cols accumulator columns of this warp's 32 lanes (adding the cross-term accumulator
+// BN columns further on, for Split).
+template <int Cols, int BN, bool Split>
+__device__ __forceinline__ void load_accumulator(uint32_t taddr, float (&v)[Cols]) {
+#pragma unroll
+    for (int g = 0; g < Cols / 32; ++g) {
+        uint32_t raw[32];
+        dev::tmem_load_32(taddr + g * 32, raw);
+        if constexpr (Split) {
+            uint32_t small[32];
+            dev::tmem_load_32(taddr + g * 32 + BN, small);
+            dev::tmem_wait_load();
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+                v[g * 32 + j] = __uint_as_float(raw[j]) + __uint_as_float(small[j]);
+            }
+        } else {
+            dev::tmem_wait_load();
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+                v[g * 32 + j] = __uint_as_float(raw[j]);
+            }
+        }
+    }
+}
+
+// alpha, bias, GELU on Cols consecutive columns starting at col0 (the reference's order,
+// src/kernels/gemm.cu:153-160). Multiplying by alpha == 1 is skipped: it is exact anyway.
+template <int Cols>
+__device__ __forceinline__ void apply_epilogue(float (&v)[Cols], const TcParams& p, int col0) {
+    if (p.alpha != 1.0F) {
+#pragma unroll
+        for (int j = 0; j < Cols; ++j) {
+            v[j] = p.alpha * v[j];
+        }
+    }
+    if (p.bias != nullptr) {
+        if (p.bias_vector_ok && col0 + Cols <= p.n) {
+            const float4* const b4 = reinterpret_cast<const float4*>(p.bias + col0);
+#pragma unroll
+            for (int q = 0; q < Cols / 4; ++q) {
+                const float4 b = __ldg(b4 + q);
+                v[4 * q] += b.x;
+                v[4 * q + 1] += b.y;
+                v[4 * q + 2] += b.z;
+                v[4 * q + 3] += b.w;
+            }
+        } else {
+#pragma unroll
+            for (int j = 0; j < Cols; ++j) {
+                if (col0 + j < p.n) {
+                    v[j] += __ldg(p.bias + col0 + j);
+                }
+            }
+        }
+    }
+    if (p.gelu) {
+#pragma unroll
+        for (int j = 0; j < Cols; ++j) {
+            v[j] = dev::gelu_erf(v[j]);
+        }
+    }
+}
+
+// One 128-byte output row per lane into the warp's slab, in the 128-byte swizzled layout a
+// TMA store reads (16-byte chunk j of row r at chunk position j ^ (r % 8)).
+template <int Cols>
+__device__ __forceinline__ void stage_row(uint8_t* slab, int lane, const float (&v)[Cols],
+                                          int c_kind) {
+    uint4* const row = reinterpret_cast<uint4*>(slab + lane * kSwizzleBytes);
+    if constexpr (Cols == 64) { // bfloat16: 8 values per 16-byte chunk
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            row[j ^ (lane & 7)] =
+                make_uint4(dev::pack_bf16x2(v[8 * j], v[8 * j + 1]),
+                           dev::pack_bf16x2(v[8 * j + 2], v[8 * j + 3]),
+                           dev::pack_bf16x2(v[8 * j + 4], v[8 * j + 5]),
+                           dev::pack_bf16x2(v[8 * j + 6], v[8 * j + 7]));
+        }
+    } else { // FP32 (optionally rounded to TF32 values): 4 values per chunk
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            float a = v[4 * j], b = v[4 * j + 1], c = v[4 * j + 2], d = v[4 * j + 3];
+            if (c_kind == 2) {
+                a = dev::round_to_tf32(a);
+                b = dev::round_to_tf32(b);
+                c = dev::round_to_tf32(c);
+                d = dev::round_to_tf32(d);
+            }
+            row[j ^ (lane & 7)] = make_uint4(__float_as_uint(a), __float_as_uint(b),
+                                             __float_as_uint(c), __float_as_uint(d));
+        }
+    }
+}
+
+// Direct global stores of 32 columns of one row (used when TMA cannot describe C).
+__device__ __forceinline__ void store_direct(const TcParams& p, long long row_offset, int col0,
+                                             const float (&v)[32]) {
+    const bool whole = p.c_vector_ok && (col0 + 32 <= p.n);
+    if (p.c_kind != 1) {
+        float* const out = static_cast<float*>(p.c) + row_offset + col0;
+        if (whole) {
+            float4* const out4 = reinterpret_cast<float4*>(out);
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+                float4 value = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+                if (p.accumulate) {
+                    const float4 old = out4[q];
+                    value.x = old.x + value.x;
+                    value.y = old.y + value.y;
+                    value.z = old.z + value.z;
+                    value.w = old.w + value.w;
+                }
+                if (p.c_kind == 2) {
+                    value.x = dev::round_to_tf32(value.x);
+                    value.y = dev::round_to_tf32(value.y);
+                    value.z = dev::round_to_tf32(value.z);
+                    value.w = dev::round_to_tf32(value.w);
+                }
+                out4[q] = value;
+            }
+        } else {
+            for (int j = 0; j < 32 && col0 + j < p.n; ++j) {
+                const float value = p.accumulate ? out[j] + v[j] : v[j];
+                out[j] = p.c_kind == 2 ? dev::round_to_tf32(value) : value;
+            }
+        }
+    } else {
+        __nv_bfloat16* const out = static_cast<__nv_bfloat16*>(p.c) + row_offset + col0;
+        if (whole) {
+            uint4* const out4 = reinterpret_cast<uint4*>(out);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                float w[8];
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    w[j] = v[8 * q + j];
+                }
+                if (p.accumulate) {
+                    const uint4 old = out4[q];
+                    const __nv_bfloat162* const pairs =
+                        reinterpret_cast<const __nv_bfloat162*>(&old);
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const float2 f = __bfloat1622float2(pairs[j]);
+                        w[2 * j] = f.x + w[2 * j];
+                        w[2 * j + 1] = f.y + w[2 * j + 1];
+                    }
+                }
+                out4[q] = make_uint4(dev::pack_bf16x2(w[0], w[1]), dev::pack_bf16x2(w[2], w[3]),
+                                     dev::pack_bf16x2(w[4], w[5]), dev::pack_bf16x2(w[6], w[7]));
+            }
+        } else {
+            for (int j = 0; j < 32 && col0 + j < p.n; ++j) {
+                const float old = p.accumulate ? __bfloat162float(out[j]) : 0.0F;
+                out[j] = __float2bfloat16_rn(p.accumulate ? old + v[j] : v[j]);
+            }
+        }
+    }
+}
+
+// Drains Cols columns of the accumulator per step through the warp's slab and TMA.
+template <int Cols, int BN, bool Split>
+__device__ __forceinline__ void epilogue_tma(const TcParams& p, const CUtensorMap* tma_c,
+                                             uint32_t tmem_cols, int first, int last, int col_base,
+                                             int row_base, int index, int outer, uint8_t* slab,
+                                             uint32_t slab_addr, int lane) {
+#pragma unroll 1
+    for (int c = first; c < last; c += Cols) {
+        const int col0 = col_base + c;
+        if (col0 >= p.n) {
+            break; // uniform across the warp
+        }
+        float v[Cols];
+        load_accumulator<Cols, BN, Split>(tmem_cols + c, v);
+        apply_epilogue<Cols>(v, p, col0);
+        // The previous chunk's store must have finished reading the slab.
+        if (lane == 0) {
+            dev::bulk_wait_group_read0();
+        }
+        __syncwarp();
+        stage_row<Cols>(slab, lane, v, p.c_kind);
+        dev::fence_proxy_async_shared();
+        __syncwarp();
+        if (lane == 0) {
+            int coords[4] = {col0, row_base, 0, 0};
+            int r = 2;
+            if (p.c_has_index) coords[r++] = index;
+            if (p.c_has_outer) coords[r++] = outer;
+            if (p.accumulate) {
+                dev::tma_store<true>(tma_c, slab_addr, p.c_rank, coords);
+            } else {
+                dev::tma_store<false>(tma_c, slab_addr, p.c_rank, coords);
+            }
+            dev::bulk_commit_group();
+        }
+    }
+}
+
 template <int ElemBytes, int BN, bool BMnMajor, bool Split>
 __global__ void __launch_bounds__(TcShape<ElemBytes, BN, Split>::kThreads, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tma_a,
-                   const __grid_constant__ CUtensorMap tma_b, const TcParams p) {
+                   const __grid_constant__ CUtensorMap tma_b,
+                   const __grid_constant__ CUtensorMap tma_c, const TcParams p) {
     using Shape = TcShape<ElemBytes, BN, Split>;
     constexpr int kStages = Shape::kStages;
     constexpr dev::MmaKind kKind = ElemBytes == 2 ? dev::MmaKind::kF16 : dev::MmaKind::kTF32;
@@ -105,12 +316,12 @@ __global__ void __launch_bounds__(TcShape<ElemBytes, BN, Split>::kThreads, 1)
     const uint32_t base = (raw_base + 1023u) & ~1023u;
     uint8_t* const smem = smem_raw + (base - raw_base);
 
-    // Stage s: [A | B | A_lo | B_lo]
+    // Stage s: [A | B | A_lo | B_lo]; then one output slab per epilogue warp; then barriers.
     const auto stage_a = [&](int s) -> uint32_t { return base + s * Shape::kStageBytes; };
     const auto stage_b = [&](int s) -> uint32_t {
         return base + s * Shape::kStageBytes + Shape::kABytes;
     };
-    const uint32_t bar_base = base + kStages * Shape::kStageBytes;
+    const uint32_t bar_base = base + Shape::kBarrierOffset;
     const auto full_bar = [&](int s) -> uint32_t { return bar_base + 8u * s; };
     const auto empty_bar = [&](int s) -> uint32_t { return bar_base + 8u * (kStages + s); };
     const auto conv_bar = [&](int s) -> uint32_t { return bar_base + 8u * (2 * kStages + s); };
@@ -120,7 +331,7 @@ __global__ void __launch_bounds__(TcShape<ElemBytes, BN, Split>::kThreads, 1)
     };
     const uint32_t drain_bar = bar_base + 8u * (3 * kStages + 4);
     uint32_t* const tmem_slot =
-        reinterpret_cast<uint32_t*>(smem + (bar_base - base) + 8 * (3 * kStages + 5));
+        reinterpret_cast<uint32_t*>(smem + Shape::kBarrierOffset + 8 * (3 * kStages + 5));
 
     const int warp = threadIdx.x / 32;
     const int lane = threadIdx.x % 32;
@@ -133,7 +344,7 @@ __global__ void __launch_bounds__(TcShape<ElemBytes, BN, Split>::kThreads, 1)
         }
         for (int a = 0; a < 2; ++a) {
             dev::mbar_init(tfull_bar(a), 1);
-            dev::mbar_init(tempty_bar(a), 128);
+            dev::mbar_init(tempty_bar(a), kEpilogueThreads);
         }
         dev::mbar_init(drain_bar, 1);
         dev::fence_barrier_init();
@@ -232,8 +443,7 @@ __global__ void __launch_bounds__(TcShape<ElemBytes, BN, Split>::kThreads, 1)
                 const uint32_t b_addr = stage_b(stage);
 #pragma unroll
                 for (int kk = 0; kk < Shape::kBlockK / Shape::kMmaK; ++kk) {
-                    const uint64_t a_desc =
-                        dev::smem_desc_sw128(a_addr + kk * 32, 16, 1024);
+                    const uint64_t a_desc = dev::smem_desc_sw128(a_addr + kk * 32, 16, 1024);
                     uint64_t b_desc;
                     if constexpr (!BMnMajor) {
                         b_desc = dev::smem_desc_sw128(b_addr + kk * 32, 16, 1024);
@@ -280,10 +490,18 @@ __global__ void __launch_bounds__(TcShape<ElemBytes, BN, Split>::kThreads, 1)
             dev::tc_commit(drain_bar);
             dev::mbar_wait(drain_bar, 0, p.status);
         }
-    } else if (warp >= 4 && warp < 8) {
+    } else if (warp >= 4 && warp < 4 + kEpilogueWarps) {
         // ---------------- epilogue ----------------
-        const int quarter = warp & 3;
-        const int row_in_tile = quarter * 32 + lane;
+        const int e = warp - 4;
+        const int quarter = warp & 3; // the TMEM lane quarter this warp may access
+        constexpr int kHalf = BN / 2;
+        const int half = e >> 2;
+        uint8_t* const slab = smem + Shape::kSlabOffset + e * kSlabBytes;
+        const uint32_t slab_addr = base + Shape::kSlabOffset + e * kSlabBytes;
+        const uint32_t lane_field = static_cast<uint32_t>(quarter * 32) << 16;
+        if (p.c_tma && lane == 0) {
+            dev::tma_prefetch_descriptor(&tma_c);
+        }
         int local = 0;
         for (int tile = blockIdx.x; tile < p.total_tiles; tile += gridDim.x, ++local) {
             const int entry = tile / per_entry;
@@ -298,125 +516,52 @@ __global__ void __launch_bounds__(TcShape<ElemBytes, BN, Split>::kThreads, 1)
                 break;
             }
             dev::tc_fence_after();
-            const int row = m_block * kBlockM + row_in_tile;
-            const bool row_ok = row < p.m;
-            const long long row_offset = static_cast<long long>(outer) * p.outer_stride_c +
-                                         static_cast<long long>(index) * p.stride_c +
-                                         static_cast<long long>(row) * p.ldc;
+            const int row_base = m_block * kBlockM + quarter * 32;
+            const uint32_t tmem_cols =
+                tmem_base + lane_field + static_cast<uint32_t>(acc * Shape::kAccColumns);
+            const int first = half * kHalf;
+            const int col_base = n_block * BN;
+            // A BF16 chunk is 64 columns (128 bytes); with BN = 64 a half tile is narrower,
+            // so that combination always takes the direct path (the host never sets c_tma).
+            if (p.c_tma && (p.c_kind != 1 || kHalf >= 64)) {
+                if (p.c_kind == 1) {
+                    epilogue_tma<64, BN, Split>(p, &tma_c, tmem_cols, first, first + kHalf,
+                                                col_base, row_base, index, outer, slab,
+                                                slab_addr, lane);
+                } else {
+                    epilogue_tma<32, BN, Split>(p, &tma_c, tmem_cols, first, first + kHalf,
+                                                col_base, row_base, index, outer, slab,
+                                                slab_addr, lane);
+                }
+            } else {
+                const int row = row_base + lane;
+                const long long row_offset = static_cast<long long>(outer) * p.outer_stride_c +
+                                             static_cast<long long>(index) * p.stride_c +
+                                             static_cast<long long>(row) * p.ldc;
 #pragma unroll 1
-            for (int chunk = 0; chunk < BN / 32; ++chunk) {
-                __syncwarp();
-                uint32_t raw[32];
-                const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
-                                       static_cast<uint32_t>(acc * Shape::kAccColumns +
-                                                             chunk * 32);
-                dev::tmem_load_32(taddr, raw);
-                if constexpr (Split) {
-                    uint32_t small[32];
-                    dev::tmem_load_32(taddr + BN, small);
-                    dev::tmem_wait_load();
-#pragma unroll
-                    for (int j = 0; j < 32; ++j) {
-                        raw[j] = __float_as_uint(__uint_as_float(raw[j]) +
-                                                 __uint_as_float(small[j]));
+                for (int c = first; c < first + kHalf; c += 32) {
+                    const int col0 = col_base + c;
+                    if (col0 >= p.n) {
+                        break;
                     }
-                } else {
-                    dev::tmem_wait_load();
-                }
-                const int col0 = n_block * BN + chunk * 32;
-                if (row_ok && col0 < p.n) {
-                float v[32];
-#pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                    v[j] = p.alpha * __uint_as_float(raw[j]);
-                }
-                if (p.bias != nullptr) {
-#pragma unroll
-                    for (int j = 0; j < 32; ++j) {
-                        if (col0 + j < p.n) {
-                            v[j] += __ldg(p.bias + col0 + j);
-                        }
+                    float v[32];
+                    load_accumulator<32, BN, Split>(tmem_cols + c, v);
+                    apply_epilogue<32>(v, p, col0);
+                    if (row < p.m) {
+                        store_direct(p, row_offset, col0, v);
                     }
-                }
-                if (p.gelu) {
-#pragma unroll
-                    for (int j = 0; j < 32; ++j) {
-                        v[j] = dev::gelu_erf(v[j]);
-                    }
-                }
-                const bool whole = p.c_vector_ok && (col0 + 32 <= p.n);
-                if (p.c_kind != 1) {
-                    float* const out = static_cast<float*>(p.c) + row_offset + col0;
-                    if (whole) {
-                        float4* const out4 = reinterpret_cast<float4*>(out);
-#pragma unroll
-                        for (int q = 0; q < 8; ++q) {
-                            float4 value = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2],
-                                                       v[4 * q + 3]);
-                            if (p.accumulate) {
-                                const float4 old = out4[q];
-                                value.x = old.x + value.x;
-                                value.y = old.y + value.y;
-                                value.z = old.z + value.z;
-                                value.w = old.w + value.w;
-                            }
-                            if (p.c_kind == 2) {
-                                value.x = dev::round_to_tf32(value.x);
-                                value.y = dev::round_to_tf32(value.y);
-                                value.z = dev::round_to_tf32(value.z);
-                                value.w = dev::round_to_tf32(value.w);
-                            }
-                            out4[q] = value;
-                        }
-                    } else {
-                        for (int j = 0; j < 32 && col0 + j < p.n; ++j) {
-                            const float value = p.accumulate ? out[j] + v[j] : v[j];
-                            out[j] = p.c_kind == 2 ? dev::round_to_tf32(value) : value;
-                        }
-                    }
-                } else {
-                    __nv_bfloat16* const out =
-                        static_cast<__nv_bfloat16*>(p.c) + row_offset + col0;
-                    if (whole) {
-                        uint4* const out4 = reinterpret_cast<uint4*>(out);
-#pragma unroll
-                        for (int q = 0; q < 4; ++q) {
-                            float w[8];
-#pragma unroll
-                            for (int j = 0; j < 8; ++j) {
-                                w[j] = v[8 * q + j];
-                            }
-                            if (p.accumulate) {
-                                const uint4 old = out4[q];
-                                const __nv_bfloat162* const pairs =
-                                    reinterpret_cast<const __nv_bfloat162*>(&old);
-#pragma unroll
-                                for (int j = 0; j < 4; ++j) {
-                                    const float2 f = __bfloat1622float2(pairs[j]);
-                                    w[2 * j] = f.x + w[2 * j];
-                                    w[2 * j + 1] = f.y + w[2 * j + 1];
-                                }
-                            }
-                            out4[q] = make_uint4(dev::pack_bf16x2(w[0], w[1]),
-                                                 dev::pack_bf16x2(w[2], w[3]),
-                                                 dev::pack_bf16x2(w[4], w[5]),
-                                                 dev::pack_bf16x2(w[6], w[7]));
-                        }
-                    } else {
-                        for (int j = 0; j < 32 && col0 + j < p.n; ++j) {
-                            const float old = p.accumulate ? __bfloat162float(out[j]) : 0.0F;
-                            out[j] = __float2bfloat16_rn(p.accumulate ? old + v[j] : v[j]);
-                        }
-                    }
-                }
+                    __syncwarp();
                 }
             }
             dev::tc_fence_before();
             dev::mbar_arrive(tempty_bar(acc));
         }
-    } else if (Split && warp >= 8) {
+        if (p.c_tma && lane == 0) {
+            dev::bulk_wait_group0();
+        }
+    } else if (Split && warp >= 4 + kEpilogueWarps) {
         // ---------------- 3xTF32 splitter ----------------
-        const int t = threadIdx.x - 256;
+        const int t = threadIdx.x - 32 * (4 + kEpilogueWarps);
         int stage = 0;
         uint32_t phase = 0;
         const int total_blocks =
@@ -428,9 +573,8 @@ __global__ void __launch_bounds__(TcShape<ElemBytes, BN, Split>::kThreads, 1)
                 break;
             }
             float4* const hi = reinterpret_cast<float4*>(smem + (stage_a(stage) - base));
-            float4* const lo =
-                reinterpret_cast<float4*>(smem + (stage_a(stage) - base) + Shape::kABytes +
-                                          Shape::kBBytes);
+            float4* const lo = reinterpret_cast<float4*>(smem + (stage_a(stage) - base) +
+                                                         Shape::kABytes + Shape::kBBytes);
             constexpr int kVectors = (Shape::kABytes + Shape::kBBytes) / 16;
 #pragma unroll 4
             for (int i = t; i < kVectors; i += 128) {

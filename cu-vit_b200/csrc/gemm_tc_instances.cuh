@@ -20,7 +20,7 @@ int launch_instance(const Plan& plan, cudaStream_t stream) {
     });
     CUVIT_TRY_CUDA(attribute_error);
     kernel<<<plan.grid, Shape::kThreads, Shape::kSmemBytes, stream>>>(plan.map_a, plan.map_b,
-                                                                       plan.params);
+                                                                       plan.map_c, plan.params);
     return host::after_launch("tc_gemm_kernel");
 }
 

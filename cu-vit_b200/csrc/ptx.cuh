@@ -129,6 +129,71 @@ __device__ __forceinline__ void tma_load(uint32_t dst, const CUtensorMap* map, u
     }
 }
 
+// Tiled store of a shared-memory box to global memory at coordinates c[0..rank) (bulk
+// group completion); with Reduce, the box is added into global memory (FP32 add in L2).
+template <bool Reduce>
+__device__ __forceinline__ void tma_store(const CUtensorMap* map, uint32_t src, int rank,
+                                          const int* c) {
+    const uint64_t desc = reinterpret_cast<uint64_t>(map);
+    if constexpr (Reduce) {
+        switch (rank) {
+        case 2:
+            asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group "
+                         "[%0, {%2, %3}], [%1];" ::"l"(desc),
+                         "r"(src), "r"(c[0]), "r"(c[1])
+                         : "memory");
+            break;
+        case 3:
+            asm volatile("cp.reduce.async.bulk.tensor.3d.global.shared::cta.add.tile.bulk_group "
+                         "[%0, {%2, %3, %4}], [%1];" ::"l"(desc),
+                         "r"(src), "r"(c[0]), "r"(c[1]), "r"(c[2])
+                         : "memory");
+            break;
+        default:
+            asm volatile("cp.reduce.async.bulk.tensor.4d.global.shared::cta.add.tile.bulk_group "
+                         "[%0, {%2, %3, %4, %5}], [%1];" ::"l"(desc),
+                         "r"(src), "r"(c[0]), "r"(c[1]), "r"(c[2]), "r"(c[3])
+                         : "memory");
+            break;
+        }
+    } else {
+        switch (rank) {
+        case 2:
+            asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group "
+                         "[%0, {%2, %3}], [%1];" ::"l"(desc),
+                         "r"(src), "r"(c[0]), "r"(c[1])
+                         : "memory");
+            break;
+        case 3:
+            asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.tile.bulk_group "
+                         "[%0, {%2, %3, %4}], [%1];" ::"l"(desc),
+                         "r"(src), "r"(c[0]), "r"(c[1]), "r"(c[2])
+                         : "memory");
+            break;
+        default:
+            asm volatile("cp.async.bulk.tensor.4d.global.shared::cta.tile.bulk_group "
+                         "[%0, {%2, %3, %4, %5}], [%1];" ::"l"(desc),
+                         "r"(src), "r"(c[0]), "r"(c[1]), "r"(c[2]), "r"(c[3])
+                         : "memory");
+            break;
+        }
+    }
+}
+
+__device__ __forceinline__ void bulk_commit_group() {
+    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+
+// Waits until the shared-memory sources of all committed bulk stores have been read.
+__device__ __forceinline__ void bulk_wait_group_read0() {
+    asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+
+// Waits until all committed bulk stores have completed.
+__device__ __forceinline__ void bulk_wait_group0() {
+    asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+
 // ---- tcgen05 ----------------------------------------------------------------------------
 
 __device__ __forceinline__ void tmem_alloc(uint32_t dst_smem, uint32_t columns) {

@@ -259,6 +259,52 @@ def test_bf16_output_and_bf16_accumulate(cuda):
     assert_close(got, existing + product, 2 ** -7, 1e-2, "bf16 accumulate")
 
 
+@pytest.mark.parametrize("math,c_dtype,n,ldc,accumulate", [
+    (kernels.MATH_BF16, kernels.DTYPE_F32, 384, 400, False),    # TMA store, padded rows
+    (kernels.MATH_BF16, kernels.DTYPE_F32, 384, 387, True),     # ldc not 16-byte: direct
+    (kernels.MATH_BF16, kernels.DTYPE_BF16, 192, 192, False),   # 64-wide tiles: direct
+    (kernels.MATH_BF16, kernels.DTYPE_BF16, 512, 520, False),   # TMA store of bf16
+    (kernels.MATH_TF32, kernels.DTYPE_TF32, 320, 320, False),   # TF32-rounded storage
+    (kernels.MATH_TF32, kernels.DTYPE_TF32, 320, 320, True),    # rounded after the add
+    (kernels.MATH_FP32, kernels.DTYPE_F32, 96, 100, True),      # reduce-add, 3xTF32
+])
+def test_output_paths(math, c_dtype, n, ldc, accumulate, cuda):
+    """Every way the epilogue writes C: TMA store, TMA reduce-add, direct stores; FP32,
+    BF16 and TF32-rounded storage; padded rows left untouched."""
+    m, k = 300, 256
+    rng = np.random.default_rng(n + ldc)
+    a = rng.standard_normal(m * k).astype(np.float32)
+    b = rng.standard_normal(n * k).astype(np.float32)
+    bias = rng.standard_normal(n).astype(np.float32)
+    if math == kernels.MATH_BF16:
+        a, b = bf16_round(a), bf16_round(b)
+    existing = rng.standard_normal(m * ldc).astype(np.float32)
+    if c_dtype == kernels.DTYPE_BF16:
+        existing = bf16_round(existing)
+    problem = GemmProblem(m=m, n=n, k=k, layout=T, ldc=ldc)
+    problem.epilogue.accumulate = accumulate
+    out_dtype = {kernels.DTYPE_F32: cuda.float32, kernels.DTYPE_TF32: cuda.float32,
+                 kernels.DTYPE_BF16: cuda.bfloat16}[c_dtype]
+    in_dtype = cuda.bfloat16 if math == kernels.MATH_BF16 else cuda.float32
+    dc = to_device(existing, out_dtype)
+    kernels.launch_gemm_ex(to_device(a, in_dtype), to_device(b, in_dtype), to_device(bias), dc,
+                           problem, c_dtype=c_dtype, math=math)
+    cuda.cuda.synchronize()
+    got = to_host(dc).reshape(m, ldc)
+    product = oracle.gemm(a, b, bias, np.zeros(m * n), m, n, k, True).reshape(m, n)
+    want = product + existing.reshape(m, ldc)[:, :n] if accumulate else product
+    np.testing.assert_array_equal(got[:, n:], existing.reshape(m, ldc)[:, n:])
+    if c_dtype == kernels.DTYPE_TF32:
+        bits = got[:, :n].view(np.uint32)
+        assert not (bits & 0x1FFF).any(), "TF32 storage holds more than 10 mantissa bits"
+    tol = {kernels.MATH_FP32: 1e-5, kernels.MATH_TF32: 4e-3, kernels.MATH_BF16: 1e-5}[math]
+    if c_dtype == kernels.DTYPE_BF16:
+        assert_close(got[:, :n], want, 2 ** -7, 1e-2, "bf16 output")
+    else:
+        scale = oracle.gemm_term_magnitudes(a, b, m, n, k, True).reshape(m, n)
+        assert_close_scaled(got[:, :n], want, scale, tol, 1e-5, "output path")
+
+
 @pytest.mark.parametrize("label", ["config1 qkv", "config1 gelu", "config1 accumulate"])
 @pytest.mark.parametrize("math", [kernels.MATH_FP32, kernels.MATH_TF32], ids=["fp32", "tf32"])
 def test_baseline_config1_against_reference_golden(label, math, golden, cuda):
