@@ -311,6 +311,347 @@ __global__ void __launch_bounds__(kThreads)
     }
 }
 
+// ---------------------------------------------------------------------------------------
+// BF16: persistent, pipelined variant. One CTA per SM walks (image, head) pairs; Q, K, V of
+// the next pair load into the second of two shared-memory buffers while the current pair is
+// in softmax. Each 128-row query tile has its own softmax warpgroup and its own 256-column
+// TMEM region (S, then P packed in its first half, then O at +128), so both tiles run at
+// once. The context is written through per-warp shared-memory slabs by TMA stores.
+//
+// Roles: warp 0 TMA loads, warp 1 MMA issue, warp 2 TMEM, warps 4..7 softmax of query tile
+// 0, warps 8..11 of query tile 1.
+// ---------------------------------------------------------------------------------------
+constexpr int kPipeThreads = 384;
+constexpr int kPipeSlabBytes = 32 * 128; // one warp's 32 context rows x 128 bytes
+
+struct PipeParams {
+    int tokens;
+    int heads;
+    int n_keys;
+    int q_tiles;
+    int pairs;        // batch * heads
+    int buffer_bytes; // one Q/K/V buffer, 1024-aligned
+    float scale;
+    float scale_log2;
+    unsigned* status;
+};
+
+__global__ void __launch_bounds__(kPipeThreads, 1)
+    attention_bf16_pipelined(const __grid_constant__ CUtensorMap map_q,
+                             const __grid_constant__ CUtensorMap map_kv,
+                             const __grid_constant__ CUtensorMap map_ctx, const PipeParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw_base = dev::smem_u32(smem_raw);
+    const uint32_t base = (raw_base + 1023u) & ~1023u;
+    uint8_t* const smem = smem_raw + (base - raw_base);
+
+    const int kv_region = p.n_keys * 128;
+    const auto q_smem = [&](int b, int t) -> uint32_t {
+        return base + b * p.buffer_bytes + t * kTileQ * 128;
+    };
+    const auto k_smem = [&](int b) -> uint32_t {
+        return base + b * p.buffer_bytes + p.q_tiles * kTileQ * 128;
+    };
+    const auto v_smem = [&](int b) -> uint32_t { return k_smem(b) + kv_region; };
+    const int slab_offset = 2 * p.buffer_bytes;
+    const uint32_t bar_base = base + slab_offset + 8 * kPipeSlabBytes;
+    // barriers: buf_full[2], buf_empty[2], s_full[2], p_full[2], o_full[2], o_free[2], drain
+    const auto bar = [&](int kind, int i) -> uint32_t { return bar_base + 8u * (2 * kind + i); };
+    constexpr int kBufFull = 0, kBufEmpty = 1, kSFull = 2, kPFull = 3, kOFull = 4, kOFree = 5;
+    const uint32_t bar_drain = bar_base + 8u * 12;
+    uint32_t* const tmem_slot =
+        reinterpret_cast<uint32_t*>(smem + slab_offset + 8 * kPipeSlabBytes + 8 * 13);
+
+    const int warp = threadIdx.x / 32;
+    const int lane = threadIdx.x % 32;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < 2; ++i) {
+            dev::mbar_init(bar(kBufFull, i), 1);
+            dev::mbar_init(bar(kBufEmpty, i), 1);
+            dev::mbar_init(bar(kSFull, i), 1);
+            dev::mbar_init(bar(kPFull, i), 128);
+            dev::mbar_init(bar(kOFull, i), 1);
+            dev::mbar_init(bar(kOFree, i), 128);
+        }
+        dev::mbar_init(bar_drain, 1);
+        dev::fence_barrier_init();
+    }
+    if (warp == 2) {
+        dev::tmem_alloc(dev::smem_u32(tmem_slot), 512);
+        dev::tmem_relinquish();
+    }
+    dev::tc_fence_before();
+    __syncthreads();
+    dev::tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0 && lane == 0) {
+        // ---------------- loads ----------------
+        dev::tma_prefetch_descriptor(&map_q);
+        dev::tma_prefetch_descriptor(&map_kv);
+        const int hd = p.heads * kHeadDim;
+        const uint32_t bytes =
+            static_cast<uint32_t>(p.q_tiles * kTileQ * 128 + 2 * kv_region);
+        int i = 0;
+        for (int pair = blockIdx.x; pair < p.pairs; pair += gridDim.x, ++i) {
+            const int b = i & 1;
+            const uint32_t use = static_cast<uint32_t>(i >> 1);
+            if (!dev::mbar_wait(bar(kBufEmpty, b), (use & 1u) ^ 1u, p.status)) {
+                break;
+            }
+            const int image = pair / p.heads;
+            const int head = pair - image * p.heads;
+            dev::mbar_arrive_expect_tx(bar(kBufFull, b), bytes);
+            for (int t = 0; t < p.q_tiles; ++t) {
+                const int c[3] = {head * kHeadDim, t * kTileQ, image};
+                dev::tma_load(q_smem(b, t), &map_q, bar(kBufFull, b), 3, c);
+            }
+            const int ck[3] = {hd + head * kHeadDim, 0, image};
+            dev::tma_load(k_smem(b), &map_kv, bar(kBufFull, b), 3, ck);
+            const int cv[3] = {2 * hd + head * kHeadDim, 0, image};
+            dev::tma_load(v_smem(b), &map_kv, bar(kBufFull, b), 3, cv);
+        }
+    } else if (warp == 1 && lane == 0) {
+        // ---------------- MMA issue ----------------
+        const uint32_t idesc_s = dev::make_idesc(1u, kTileQ, p.n_keys, false, false);
+        constexpr uint32_t kIdescO = dev::make_idesc(1u, kTileQ, kHeadDim, false, true);
+        bool ok = true;
+        int i = 0;
+        for (int pair = blockIdx.x; pair < p.pairs && ok; pair += gridDim.x, ++i) {
+            const int b = i & 1;
+            const uint32_t use = static_cast<uint32_t>(i >> 1);
+            const uint32_t parity = static_cast<uint32_t>(i & 1);
+            if (!dev::mbar_wait(bar(kBufFull, b), use & 1u, p.status)) {
+                ok = false;
+                break;
+            }
+            for (int t = 0; t < p.q_tiles && ok; ++t) {
+                // The previous pair's O_t must have been read out of this TMEM region.
+                if (!dev::mbar_wait(bar(kOFree, t), parity ^ 1u, p.status)) {
+                    ok = false;
+                    break;
+                }
+                dev::tc_fence_after();
+                const uint32_t s_tmem = tmem + static_cast<uint32_t>(256 * t);
+#pragma unroll
+                for (int kk = 0; kk < kHeadDim / 16; ++kk) {
+                    const uint64_t a_desc =
+                        dev::smem_desc_sw128(q_smem(b, t) + kk * 32, 16, 1024);
+                    const uint64_t b_desc = dev::smem_desc_sw128(k_smem(b) + kk * 32, 16, 1024);
+                    dev::mma_ss<dev::MmaKind::kF16>(s_tmem, a_desc, b_desc, idesc_s,
+                                                    kk > 0 ? 1u : 0u);
+                }
+                dev::tc_commit(bar(kSFull, t));
+            }
+            for (int t = 0; t < p.q_tiles && ok; ++t) {
+                if (!dev::mbar_wait(bar(kPFull, t), parity, p.status)) {
+                    ok = false;
+                    break;
+                }
+                dev::tc_fence_after();
+                const uint32_t region = tmem + static_cast<uint32_t>(256 * t);
+                const int steps = p.n_keys / 16;
+                for (int kk = 0; kk < steps; ++kk) {
+                    const uint64_t b_desc =
+                        dev::smem_desc_sw128(v_smem(b) + kk * 16 * 128, kv_region, 1024);
+                    dev::mma_ts<dev::MmaKind::kF16>(region + 128, region + kk * 8, b_desc,
+                                                    kIdescO, kk > 0 ? 1u : 0u);
+                }
+                dev::tc_commit(bar(kOFull, t));
+            }
+            if (ok) {
+                dev::tc_commit(bar(kBufEmpty, b)); // both tiles' MMAs have read buffer b
+            }
+        }
+        if (!ok) {
+            dev::tc_commit(bar_drain);
+            dev::mbar_wait(bar_drain, 0, p.status);
+        }
+    } else if (warp >= 4) {
+        // ---------------- softmax and output, one warpgroup per query tile ----------------
+        const int t = (warp - 4) >> 2;
+        const int quarter = warp & 3;
+        const int row = quarter * 32 + lane;
+        const uint32_t lane_field = static_cast<uint32_t>(quarter * 32) << 16;
+        const uint32_t region = tmem + lane_field + static_cast<uint32_t>(256 * t);
+        uint8_t* const slab = smem + slab_offset + (warp - 4) * kPipeSlabBytes;
+        const uint32_t slab_addr = base + slab_offset + (warp - 4) * kPipeSlabBytes;
+        const int chunks = (p.n_keys + 31) / 32;
+        if (t < p.q_tiles) {
+            if (lane == 0) {
+                dev::tma_prefetch_descriptor(&map_ctx);
+            }
+            int i = 0;
+            for (int pair = blockIdx.x; pair < p.pairs; pair += gridDim.x, ++i) {
+                const uint32_t parity = static_cast<uint32_t>(i & 1);
+                if (!dev::mbar_wait(bar(kSFull, t), parity, p.status)) {
+                    break;
+                }
+                dev::tc_fence_after();
+                float maximum = -INFINITY;
+                for (int c = 0; c < chunks; ++c) {
+                    uint32_t s[32];
+                    dev::tmem_load_32(region + c * 32, s);
+                    dev::tmem_wait_load();
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        if (c * 32 + j < p.tokens) {
+                            maximum = fmaxf(maximum, __uint_as_float(s[j]) * p.scale);
+                        }
+                    }
+                }
+                const float offset = maximum * 1.4426950408889634F;
+                float sum = 0.0F;
+                for (int c = 0; c < chunks; ++c) {
+                    uint32_t s[32];
+                    dev::tmem_load_32(region + c * 32, s);
+                    dev::tmem_wait_load();
+                    uint32_t packed[16];
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        const int key = c * 32 + 2 * j;
+                        const float e0 = key < p.tokens
+                                             ? dev::ex2_approx(fmaf(__uint_as_float(s[2 * j]),
+                                                                    p.scale_log2, -offset))
+                                             : 0.0F;
+                        const float e1 = key + 1 < p.tokens
+                                             ? dev::ex2_approx(fmaf(__uint_as_float(s[2 * j + 1]),
+                                                                    p.scale_log2, -offset))
+                                             : 0.0F;
+                        packed[j] = dev::pack_bf16x2(e0, e1);
+                        const float2 rounded =
+                            __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&packed[j]));
+                        sum += rounded.x + rounded.y;
+                    }
+                    dev::tmem_store_16(region + c * 16, packed);
+                }
+                dev::tmem_wait_store();
+                dev::tc_fence_before();
+                dev::mbar_arrive(bar(kPFull, t));
+                if (!dev::mbar_wait(bar(kOFull, t), parity, p.status)) {
+                    break;
+                }
+                dev::tc_fence_after();
+                uint32_t o0[32];
+                uint32_t o1[32];
+                dev::tmem_load_32(region + 128, o0);
+                dev::tmem_load_32(region + 160, o1);
+                dev::tmem_wait_load();
+                dev::tc_fence_before();
+                dev::mbar_arrive(bar(kOFree, t)); // this TMEM region may take the next S
+                const float inverse = 1.0F / sum;
+                if (lane == 0) {
+                    dev::bulk_wait_group_read0(); // the slab's previous store has been read
+                }
+                __syncwarp();
+                uint4* const slab_row = reinterpret_cast<uint4*>(slab + lane * 128);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    const uint32_t* const o = j < 4 ? o0 : o1;
+                    const int base_j = (j & 3) * 8;
+                    slab_row[j ^ (lane & 7)] = make_uint4(
+                        dev::pack_bf16x2(__uint_as_float(o[base_j]) * inverse,
+                                         __uint_as_float(o[base_j + 1]) * inverse),
+                        dev::pack_bf16x2(__uint_as_float(o[base_j + 2]) * inverse,
+                                         __uint_as_float(o[base_j + 3]) * inverse),
+                        dev::pack_bf16x2(__uint_as_float(o[base_j + 4]) * inverse,
+                                         __uint_as_float(o[base_j + 5]) * inverse),
+                        dev::pack_bf16x2(__uint_as_float(o[base_j + 6]) * inverse,
+                                         __uint_as_float(o[base_j + 7]) * inverse));
+                }
+                dev::fence_proxy_async_shared();
+                __syncwarp();
+                if (lane == 0) {
+                    const int image = pair / p.heads;
+                    const int head = pair - image * p.heads;
+                    const int coords[3] = {head * kHeadDim, t * kTileQ + quarter * 32, image};
+                    dev::tma_store<false>(&map_ctx, slab_addr, 3, coords);
+                    dev::bulk_commit_group();
+                }
+                (void)row;
+            }
+            if (lane == 0) {
+                dev::bulk_wait_group0();
+            }
+        }
+    }
+
+    __syncthreads();
+    if (warp == 2) {
+        dev::tc_fence_after();
+        dev::tmem_dealloc(tmem, 512);
+    }
+}
+
+int launch_bf16_pipelined(const void* qkv, void* context, int batch, int tokens, int heads,
+                          float scale, const host::DeviceContext& device, cudaStream_t stream) {
+    const int n_keys = (tokens + 15) / 16 * 16;
+    const int q_tiles = (tokens + kTileQ - 1) / kTileQ;
+    const int row = 3 * heads * kHeadDim;
+    const int e = heads * kHeadDim;
+
+    host::TmaTensor tq;
+    tq.base = qkv;
+    tq.type = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+    tq.element_bytes = 2;
+    tq.rank = 3;
+    tq.dims[0] = static_cast<uint64_t>(row);
+    tq.dims[1] = static_cast<uint64_t>(tokens);
+    tq.dims[2] = static_cast<uint64_t>(batch);
+    tq.strides_bytes[0] = static_cast<uint64_t>(row) * 2;
+    tq.strides_bytes[1] = static_cast<uint64_t>(row) * tokens * 2;
+    tq.box[0] = 64;
+    tq.box[1] = kTileQ;
+    tq.box[2] = 1;
+    host::TmaTensor tkv = tq;
+    tkv.box[1] = static_cast<uint32_t>(n_keys);
+    host::TmaTensor tc;
+    tc.base = context;
+    tc.type = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+    tc.element_bytes = 2;
+    tc.rank = 3;
+    tc.dims[0] = static_cast<uint64_t>(e);
+    tc.dims[1] = static_cast<uint64_t>(tokens);
+    tc.dims[2] = static_cast<uint64_t>(batch);
+    tc.strides_bytes[0] = static_cast<uint64_t>(e) * 2;
+    tc.strides_bytes[1] = static_cast<uint64_t>(e) * tokens * 2;
+    tc.box[0] = 64;
+    tc.box[1] = 32;
+    tc.box[2] = 1;
+
+    CUtensorMap map_q;
+    CUtensorMap map_kv;
+    CUtensorMap map_ctx;
+    CUVIT_TRY(host::encode_tma(tq, &map_q));
+    CUVIT_TRY(host::encode_tma(tkv, &map_kv));
+    CUVIT_TRY(host::encode_tma(tc, &map_ctx));
+
+    PipeParams params;
+    params.tokens = tokens;
+    params.heads = heads;
+    params.n_keys = n_keys;
+    params.q_tiles = q_tiles;
+    params.pairs = batch * heads;
+    params.buffer_bytes = (q_tiles * kTileQ * 128 + 2 * n_keys * 128 + 1023) / 1024 * 1024;
+    params.scale = scale;
+    params.scale_log2 = scale * 1.4426950408889634F;
+    params.status = device.status;
+
+    const int smem = 1024 + 2 * params.buffer_bytes + 8 * kPipeSlabBytes + 8 * 13 + 16;
+    auto* kernel = &attention_bf16_pipelined;
+    static std::once_flag once;
+    static cudaError_t attribute_error = cudaSuccess;
+    std::call_once(once, [kernel]() {
+        attribute_error = cudaFuncSetAttribute(
+            kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    });
+    CUVIT_TRY_CUDA(attribute_error);
+    const int grid = params.pairs < device.sm_count ? params.pairs : device.sm_count;
+    kernel<<<grid, kPipeThreads, smem, stream>>>(map_q, map_kv, map_ctx, params);
+    return host::after_launch("attention_bf16_pipelined");
+}
+
 template <int ElemBytes>
 int launch_typed(const void* qkv, void* context, int batch, int tokens, int heads, float scale,
                  bool round_output, const host::DeviceContext& device, cudaStream_t stream) {
@@ -409,8 +750,8 @@ extern "C" int cuvit_attention(const void* qkv, void* context, int dtype, int ba
     }
     const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
     if (dtype == CUVIT_DTYPE_BF16) {
-        return cuvit::attn::launch_typed<2>(qkv, context, batch, tokens, heads, scale, false,
-                                            *device, s);
+        return cuvit::attn::launch_bf16_pipelined(qkv, context, batch, tokens, heads, scale,
+                                                  *device, s);
     }
     return cuvit::attn::launch_typed<4>(qkv, context, batch, tokens, heads, scale,
                                         dtype == CUVIT_DTYPE_TF32, *device, s);

@@ -152,9 +152,16 @@ __device__ __forceinline__ void apply_epilogue(float (&v)[Cols], const TcParams&
         }
     }
     if (p.gelu) {
+        if (p.c_kind == 1) {
 #pragma unroll
-        for (int j = 0; j < Cols; ++j) {
-            v[j] = dev::gelu_erf(v[j]);
+            for (int j = 0; j < Cols; ++j) {
+                v[j] = dev::gelu_bf16_output(v[j]);
+            }
+        } else {
+#pragma unroll
+            for (int j = 0; j < Cols; ++j) {
+                v[j] = dev::gelu_erf(v[j]);
+            }
         }
     }
 }

@@ -370,6 +370,36 @@ __device__ __forceinline__ float round_to_tf32(float x) {
     return __uint_as_float(rounded);
 }
 
+__device__ __forceinline__ float ex2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+__device__ __forceinline__ float rcp_approx(float x) {
+    float y;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+// GELU with erf evaluated by Abramowitz & Stegun, Handbook of Mathematical Functions,
+// formula 7.1.26 (|error| <= 1.5e-7 on erf), using the hardware reciprocal and exponential.
+// For BF16 outputs, whose rounding (2^-9 relative) is far coarser than the approximation;
+// FP32 and TF32 outputs keep gelu_erf.
+__device__ __forceinline__ float gelu_bf16_output(float x) {
+    const float z = fabsf(x) * 0.7071067811865475F;
+    const float t = rcp_approx(fmaf(0.3275911F, z, 1.0F));
+    float poly = fmaf(t, 1.061405429F, -1.453152027F);
+    poly = fmaf(t, poly, 1.421413741F);
+    poly = fmaf(t, poly, -0.284496736F);
+    poly = fmaf(t, poly, 0.254829592F);
+    poly *= t;
+    const float tail = ex2_approx(-(z * z) * 1.4426950408889634F);
+    const float erf_abs = fmaf(-poly, tail, 1.0F);
+    const float half_x = 0.5F * x;
+    return fmaf(half_x, copysignf(erf_abs, x), half_x);
+}
+
 __device__ __forceinline__ uint32_t pack_bf16x2(float low, float high) {
     const __nv_bfloat162 pair = __floats2bfloat162_rn(low, high);
     return *reinterpret_cast<const uint32_t*>(&pair);

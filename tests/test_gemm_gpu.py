@@ -195,6 +195,26 @@ def test_gelu_epilogue_and_bias_order(math, cuda):
     assert diff.any(), "the GELU epilogue applied the bias in the wrong order"
 
 
+def test_gelu_epilogue_with_bf16_output(cuda):
+    """FC1's form: bf16 operands, bias + GELU, bf16 output (the epilogue evaluates erf with
+    Abramowitz-Stegun 7.1.26 here): within bf16 rounding of the erf-form oracle."""
+    m, n, k = 200, 768, 192
+    rng = np.random.default_rng(606)
+    a = bf16_round(rng.standard_normal(m * k))
+    b = bf16_round(0.2 * rng.standard_normal(n * k))
+    bias = rng.standard_normal(n).astype(np.float32)
+    want = oracle.gemm(a, b, bias, np.zeros(m * n), m, n, k, True, gelu=True)
+    problem = gemm_problem(m, n, k, T)
+    problem.epilogue.gelu = True
+    got = run(a, b, bias, np.zeros(m * n), problem, kernels.MATH_BF16, cuda,
+              c_dtype=kernels.DTYPE_BF16)
+    assert_close(got, want, 2 ** -8, 1e-3, "bf16 GELU epilogue")
+    # the approximation itself, away from bf16 rounding: FP32-output path vs bf16-output
+    # path differ only by the final rounding
+    got32 = run(a, b, bias, np.zeros(m * n), problem, kernels.MATH_BF16, cuda)
+    np.testing.assert_allclose(got, bf16_round(got32), rtol=2 ** -7, atol=1e-6)
+
+
 def test_zero_k_produces_the_bias_exactly(cuda):
     m, n = 8, 8
     bias = np.random.default_rng(5).standard_normal(n).astype(np.float32)
