@@ -110,6 +110,10 @@ __global__ void __launch_bounds__(kThreads)
     __syncthreads();
     dev::tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    // Inputs of this launch may come from the previous one: nothing global is read or
+    // written before it has finished.
+    dev::grid_dependency_wait();
+    dev::grid_launch_dependents();
 
     if (warp == 0 && lane == 0) {
         // ---------------- loads and MMA issue ----------------
@@ -385,6 +389,10 @@ __global__ void __launch_bounds__(kPipeThreads, 1)
     __syncthreads();
     dev::tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    // Inputs of this launch may come from the previous one: nothing global is read or
+    // written before it has finished.
+    dev::grid_dependency_wait();
+    dev::grid_launch_dependents();
 
     if (warp == 0 && lane == 0) {
         // ---------------- loads ----------------
@@ -477,7 +485,6 @@ __global__ void __launch_bounds__(kPipeThreads, 1)
         const uint32_t region = tmem + lane_field + static_cast<uint32_t>(256 * t);
         uint8_t* const slab = smem + slab_offset + (warp - 4) * kPipeSlabBytes;
         const uint32_t slab_addr = base + slab_offset + (warp - 4) * kPipeSlabBytes;
-        const int chunks = (p.n_keys + 31) / 32;
         if (t < p.q_tiles) {
             if (lane == 0) {
                 dev::tma_prefetch_descriptor(&map_ctx);
@@ -489,44 +496,99 @@ __global__ void __launch_bounds__(kPipeThreads, 1)
                     break;
                 }
                 dev::tc_fence_after();
-                float maximum = -INFINITY;
-                for (int c = 0; c < chunks; ++c) {
-                    uint32_t s[32];
-                    dev::tmem_load_32(region + c * 32, s);
-                    dev::tmem_wait_load();
+                // A warp whose 32 query rows all lie past the token count has nothing to
+                // compute: its O rows are clipped by the context store.
+                const bool live = t * kTileQ + quarter * 32 < p.tokens;
+                float sum = 1.0F;
+                if (live) {
+                    // Two 32-column TMEM loads in flight per wait; chunk indices are
+                    // compile-time (the region is 256 columns wide), so the loaded values stay
+                    // in registers. Columns at or past n_keys are masked like padded keys.
+                    // The row extreme of the raw scores: the maximum for a positive scale, the
+                    // minimum for a negative one; scale is applied once, to the extreme.
+                    const bool positive = p.scale >= 0.0F;
+                    float extreme = positive ? -INFINITY : INFINITY;
+                    const auto reduce = [&](const uint32_t(&s)[32], int c) {
+                        if ((c + 1) * 32 <= p.tokens) { // whole chunk of real keys
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) {
-                        if (c * 32 + j < p.tokens) {
-                            maximum = fmaxf(maximum, __uint_as_float(s[j]) * p.scale);
+                            for (int j = 0; j < 32; ++j) {
+                                extreme = positive ? fmaxf(extreme, __uint_as_float(s[j]))
+                                                   : fminf(extreme, __uint_as_float(s[j]));
+                            }
+                        } else {
+#pragma unroll
+                            for (int j = 0; j < 32; ++j) {
+                                if (c * 32 + j < p.tokens) {
+                                    extreme = positive ? fmaxf(extreme, __uint_as_float(s[j]))
+                                                       : fminf(extreme, __uint_as_float(s[j]));
+                                }
+                            }
                         }
-                    }
-                }
-                const float offset = maximum * 1.4426950408889634F;
-                float sum = 0.0F;
-                for (int c = 0; c < chunks; ++c) {
-                    uint32_t s[32];
-                    dev::tmem_load_32(region + c * 32, s);
-                    dev::tmem_wait_load();
-                    uint32_t packed[16];
+                    };
 #pragma unroll
-                    for (int j = 0; j < 16; ++j) {
-                        const int key = c * 32 + 2 * j;
-                        const float e0 = key < p.tokens
-                                             ? dev::ex2_approx(fmaf(__uint_as_float(s[2 * j]),
-                                                                    p.scale_log2, -offset))
-                                             : 0.0F;
-                        const float e1 = key + 1 < p.tokens
-                                             ? dev::ex2_approx(fmaf(__uint_as_float(s[2 * j + 1]),
-                                                                    p.scale_log2, -offset))
-                                             : 0.0F;
-                        packed[j] = dev::pack_bf16x2(e0, e1);
-                        const float2 rounded =
-                            __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&packed[j]));
-                        sum += rounded.x + rounded.y;
+                    for (int c = 0; c < 8; c += 2) {
+                        if (c * 32 >= p.n_keys) {
+                            break;
+                        }
+                        uint32_t s0[32];
+                        uint32_t s1[32];
+                        dev::tmem_load_32(region + c * 32, s0);
+                        dev::tmem_load_32(region + (c + 1) * 32, s1);
+                        dev::tmem_wait_load();
+                        reduce(s0, c);
+                        reduce(s1, c + 1);
                     }
-                    dev::tmem_store_16(region + c * 16, packed);
+                    const float offset = extreme * p.scale_log2;
+                    sum = 0.0F;
+                    // P = exp(scale * s - max), packed to bf16 pairs in place; the row sum is
+                    // taken over the FP32 values.
+                    const auto exp_pack = [&](const uint32_t(&s)[32], int c) {
+                        uint32_t packed[16];
+                        if ((c + 1) * 32 <= p.tokens) {
+#pragma unroll
+                            for (int j = 0; j < 16; ++j) {
+                                const float e0 = dev::ex2_approx(
+                                    fmaf(__uint_as_float(s[2 * j]), p.scale_log2, -offset));
+                                const float e1 = dev::ex2_approx(
+                                    fmaf(__uint_as_float(s[2 * j + 1]), p.scale_log2, -offset));
+                                sum += e0 + e1;
+                                packed[j] = dev::pack_bf16x2(e0, e1);
+                            }
+                        } else {
+#pragma unroll
+                            for (int j = 0; j < 16; ++j) {
+                                const int key = c * 32 + 2 * j;
+                                float e0 = 0.0F;
+                                float e1 = 0.0F;
+                                if (key < p.tokens) {
+                                    e0 = dev::ex2_approx(
+                                        fmaf(__uint_as_float(s[2 * j]), p.scale_log2, -offset));
+                                }
+                                if (key + 1 < p.tokens) {
+                                    e1 = dev::ex2_approx(fmaf(__uint_as_float(s[2 * j + 1]),
+                                                              p.scale_log2, -offset));
+                                }
+                                sum += e0 + e1;
+                                packed[j] = dev::pack_bf16x2(e0, e1);
+                            }
+                        }
+                        dev::tmem_store_16(region + c * 16, packed);
+                    };
+#pragma unroll
+                    for (int c = 0; c < 8; c += 2) {
+                        if (c * 32 >= p.n_keys) {
+                            break;
+                        }
+                        uint32_t s0[32];
+                        uint32_t s1[32];
+                        dev::tmem_load_32(region + c * 32, s0);
+                        dev::tmem_load_32(region + (c + 1) * 32, s1);
+                        dev::tmem_wait_load();
+                        exp_pack(s0, c);
+                        exp_pack(s1, c + 1);
+                    }
+                    dev::tmem_wait_store();
                 }
-                dev::tmem_wait_store();
                 dev::tc_fence_before();
                 dev::mbar_arrive(bar(kPFull, t));
                 if (!dev::mbar_wait(bar(kOFull, t), parity, p.status)) {
@@ -648,7 +710,7 @@ int launch_bf16_pipelined(const void* qkv, void* context, int batch, int tokens,
     });
     CUVIT_TRY_CUDA(attribute_error);
     const int grid = params.pairs < device.sm_count ? params.pairs : device.sm_count;
-    kernel<<<grid, kPipeThreads, smem, stream>>>(map_q, map_kv, map_ctx, params);
+    host::pdl_launch(kernel, grid, kPipeThreads, smem, stream, map_q, map_kv, map_ctx, params);
     return host::after_launch("attention_bf16_pipelined");
 }
 
@@ -710,7 +772,8 @@ int launch_typed(const void* qkv, void* context, int batch, int tokens, int head
             kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
     });
     CUVIT_TRY_CUDA(attribute_error);
-    kernel<<<batch * heads, kThreads, smem, stream>>>(map_q, map_kv, map_v, params);
+    host::pdl_launch(kernel, batch * heads, kThreads, smem, stream, map_q, map_kv, map_v,
+                     params);
     return host::after_launch("attention_kernel");
 }
 

@@ -88,6 +88,8 @@ __global__ void __launch_bounds__(kThreads)
                            const float* __restrict__ gamma, const float* __restrict__ beta,
                            Out* __restrict__ output, long long out_stride, int rows, int columns,
                            float epsilon) {
+    dev::grid_dependency_wait();
+    dev::grid_launch_dependents();
     const int row = blockIdx.x * kRowsPerBlock + threadIdx.x / kWarp;
     const int lane = threadIdx.x % kWarp;
     if (row >= rows) {
@@ -160,6 +162,8 @@ __global__ void __launch_bounds__(kThreads)
                             const float* __restrict__ gamma, const float* __restrict__ beta,
                             Out* __restrict__ output, long long out_stride, int columns,
                             float epsilon) {
+    dev::grid_dependency_wait();
+    dev::grid_launch_dependents();
     __shared__ float scratch[kThreads / kWarp];
     const long long row = blockIdx.x;
     const float* const x = input + row * in_stride;
@@ -188,6 +192,8 @@ __global__ void __launch_bounds__(kThreads)
 __global__ void __launch_bounds__(kThreads)
     softmax_warp_kernel(const float* input, float* output, int rows, int columns,
                         long long stride) {
+    dev::grid_dependency_wait();
+    dev::grid_launch_dependents();
     const int row = blockIdx.x * kRowsPerBlock + threadIdx.x / kWarp;
     const int lane = threadIdx.x % kWarp;
     if (row >= rows) {
@@ -223,6 +229,8 @@ __global__ void __launch_bounds__(kThreads)
 
 __global__ void __launch_bounds__(kThreads)
     softmax_block_kernel(const float* input, float* output, int columns, long long stride) {
+    dev::grid_dependency_wait();
+    dev::grid_launch_dependents();
     __shared__ float scratch[kThreads / kWarp];
     __shared__ float shared_max;
     const long long row = blockIdx.x;
@@ -260,6 +268,8 @@ __global__ void __launch_bounds__(kThreads)
 
 __global__ void gelu_kernel(const float* __restrict__ input, float* __restrict__ output,
                             long long count, int vectorised) {
+    dev::grid_dependency_wait();
+    dev::grid_launch_dependents();
     const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
     long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (vectorised) {
@@ -283,6 +293,8 @@ __global__ void gelu_kernel(const float* __restrict__ input, float* __restrict__
 
 __global__ void add_kernel(float* __restrict__ accumulator, const float* __restrict__ addend,
                            long long count, int vectorised) {
+    dev::grid_dependency_wait();
+    dev::grid_launch_dependents();
     const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
     long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (vectorised) {
@@ -311,6 +323,8 @@ __global__ void add_kernel(float* __restrict__ accumulator, const float* __restr
 __global__ void add_broadcast_kernel(float* __restrict__ accumulator,
                                      const float* __restrict__ addend, long long count,
                                      long long total) {
+    dev::grid_dependency_wait();
+    dev::grid_launch_dependents();
     const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
     for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
          i += stride) {
@@ -321,6 +335,8 @@ __global__ void add_broadcast_kernel(float* __restrict__ accumulator,
 __global__ void broadcast_kernel(float* __restrict__ destination,
                                  const float* __restrict__ source, long long count,
                                  long long destination_stride, long long total) {
+    dev::grid_dependency_wait();
+    dev::grid_launch_dependents();
     const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
     for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
          i += stride) {
@@ -334,6 +350,8 @@ __global__ void broadcast_kernel(float* __restrict__ destination,
 __global__ void init_tokens_kernel(float* __restrict__ tokens, const float* __restrict__ cls,
                                    const float* __restrict__ pos, long long per_image,
                                    int embed, long long total, int vectorised) {
+    dev::grid_dependency_wait();
+    dev::grid_launch_dependents();
     const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
     long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (vectorised) {
@@ -359,6 +377,8 @@ __global__ void init_tokens_kernel(float* __restrict__ tokens, const float* __re
 
 __global__ void convert_bf16_kernel(const float* __restrict__ input,
                                     __nv_bfloat16* __restrict__ output, long long count) {
+    dev::grid_dependency_wait();
+    dev::grid_launch_dependents();
     const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
     for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < count;
          i += stride) {
@@ -367,6 +387,8 @@ __global__ void convert_bf16_kernel(const float* __restrict__ input,
 }
 
 __global__ void round_tf32_kernel(const float* input, float* output, long long count) {
+    dev::grid_dependency_wait();
+    dev::grid_launch_dependents();
     const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
     for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < count;
          i += stride) {
@@ -380,6 +402,8 @@ template <typename Out, int Vec>
 __global__ void extract_patches_kernel(const float* __restrict__ images, Out* __restrict__ patches,
                                        int channels, int height, int width, int patch,
                                        int across, int per_image, long long total) {
+    dev::grid_dependency_wait();
+    dev::grid_launch_dependents();
     const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
     const int area = patch * patch;
     const int row_length = channels * area;
@@ -450,11 +474,11 @@ int layer_norm_impl(const float* input, long long in_stride, const float* gamma,
         if (fast) {
             const unsigned blocks =
                 static_cast<unsigned>((rows + kRowsPerBlock - 1) / kRowsPerBlock);
-            layer_norm_warp_kernel<Out><<<blocks, kThreads, 0, stream>>>(
-                input, in_stride, gamma, beta, out, out_stride, rows, columns, epsilon);
+            host::pdl_launch(layer_norm_warp_kernel<Out>, blocks, kThreads, 0, stream, input,
+                             in_stride, gamma, beta, out, out_stride, rows, columns, epsilon);
         } else {
-            layer_norm_block_kernel<Out><<<rows, kThreads, 0, stream>>>(
-                input, in_stride, gamma, beta, out, out_stride, columns, epsilon);
+            host::pdl_launch(layer_norm_block_kernel<Out>, rows, kThreads, 0, stream, input,
+                             in_stride, gamma, beta, out, out_stride, columns, epsilon);
         }
     };
     if (out_dtype == CUVIT_DTYPE_BF16) {
@@ -486,9 +510,11 @@ int softmax_impl(const float* input, float* output, int rows, int columns, long 
     }
     if (columns <= kWarp * kMaxSoftmaxPerLane) {
         const unsigned blocks = static_cast<unsigned>((rows + kRowsPerBlock - 1) / kRowsPerBlock);
-        softmax_warp_kernel<<<blocks, kThreads, 0, stream>>>(input, output, rows, columns, stride);
+        host::pdl_launch(softmax_warp_kernel, blocks, kThreads, 0, stream, input, output, rows,
+                         columns, stride);
     } else {
-        softmax_block_kernel<<<rows, kThreads, 0, stream>>>(input, output, columns, stride);
+        host::pdl_launch(softmax_block_kernel, rows, kThreads, 0, stream, input, output,
+                         columns, stride);
     }
     return host::after_launch("softmax");
 }
@@ -526,11 +552,13 @@ int extract_patches_impl(const float* images, void* patches, int out_dtype, int 
     const auto run = [&](auto* out) {
         using Out = std::remove_pointer_t<decltype(out)>;
         if (vec) {
-            extract_patches_kernel<Out, 4><<<blocks, kThreads, 0, stream>>>(
-                images, out, channels, height, width, patch, across, per_image, total);
+            host::pdl_launch(extract_patches_kernel<Out, 4>, blocks, kThreads, 0, stream,
+                             images, out, channels, height, width, patch, across, per_image,
+                             total);
         } else {
-            extract_patches_kernel<Out, 1><<<blocks, kThreads, 0, stream>>>(
-                images, out, channels, height, width, patch, across, per_image, total);
+            host::pdl_launch(extract_patches_kernel<Out, 1>, blocks, kThreads, 0, stream,
+                             images, out, channels, height, width, patch, across, per_image,
+                             total);
         }
     };
     if (bf16) {
@@ -593,8 +621,8 @@ int cuvit_gelu(const float* input, float* output, int64_t count, cuvit_stream_t 
         return fail(CUVIT_LENGTH_ERROR, "Elementwise launch exceeds the CUDA grid limit");
     }
     const int vec = aligned(input, 16) && aligned(output, 16) ? 1 : 0;
-    gelu_kernel<<<static_cast<unsigned>(grid), kThreads, 0,
-                  reinterpret_cast<cudaStream_t>(stream)>>>(input, output, count, vec);
+    cuvit::host::pdl_launch(gelu_kernel, static_cast<unsigned>(grid), kThreads, 0,
+                            reinterpret_cast<cudaStream_t>(stream), input, output, count, vec);
     return cuvit::host::after_launch("gelu");
 }
 
@@ -613,8 +641,9 @@ int cuvit_add(float* accumulator, const float* addend, int64_t count, cuvit_stre
         return fail(CUVIT_LENGTH_ERROR, "Elementwise launch exceeds the CUDA grid limit");
     }
     const int vec = aligned(accumulator, 16) && aligned(addend, 16) ? 1 : 0;
-    add_kernel<<<static_cast<unsigned>(grid), kThreads, 0,
-                 reinterpret_cast<cudaStream_t>(stream)>>>(accumulator, addend, count, vec);
+    cuvit::host::pdl_launch(add_kernel, static_cast<unsigned>(grid), kThreads, 0,
+                            reinterpret_cast<cudaStream_t>(stream), accumulator, addend, count,
+                            vec);
     return cuvit::host::after_launch("add");
 }
 
@@ -634,9 +663,9 @@ int cuvit_add_broadcast(float* accumulator, const float* addend, int64_t count, 
     if (grid < 0) {
         return fail(CUVIT_LENGTH_ERROR, "Elementwise launch exceeds the CUDA grid limit");
     }
-    add_broadcast_kernel<<<static_cast<unsigned>(grid), kThreads, 0,
-                           reinterpret_cast<cudaStream_t>(stream)>>>(accumulator, addend, count,
-                                                                     total);
+    cuvit::host::pdl_launch(add_broadcast_kernel, static_cast<unsigned>(grid), kThreads, 0,
+                            reinterpret_cast<cudaStream_t>(stream), accumulator, addend, count,
+                            total);
     return cuvit::host::after_launch("add_broadcast");
 }
 
@@ -656,9 +685,9 @@ int cuvit_broadcast(float* destination, const float* source, int64_t count,
     if (grid < 0) {
         return fail(CUVIT_LENGTH_ERROR, "Elementwise launch exceeds the CUDA grid limit");
     }
-    broadcast_kernel<<<static_cast<unsigned>(grid), kThreads, 0,
-                       reinterpret_cast<cudaStream_t>(stream)>>>(destination, source, count,
-                                                                 destination_stride, total);
+    cuvit::host::pdl_launch(broadcast_kernel, static_cast<unsigned>(grid), kThreads, 0,
+                            reinterpret_cast<cudaStream_t>(stream), destination, source, count,
+                            destination_stride, total);
     return cuvit::host::after_launch("broadcast");
 }
 
@@ -696,9 +725,9 @@ int cuvit_init_tokens(float* tokens, const float* class_token, const float* posi
                             aligned(position, 16)
                         ? 1
                         : 0;
-    init_tokens_kernel<<<static_cast<unsigned>(grid), kThreads, 0,
-                         reinterpret_cast<cudaStream_t>(stream)>>>(
-        tokens, class_token, position, per_image, embed, total, vec);
+    cuvit::host::pdl_launch(init_tokens_kernel, static_cast<unsigned>(grid), kThreads, 0,
+                            reinterpret_cast<cudaStream_t>(stream), tokens, class_token, position,
+                            per_image, embed, total, vec);
     return cuvit::host::after_launch("init_tokens");
 }
 
@@ -714,9 +743,9 @@ int cuvit_convert_f32_to_bf16(const float* input, void* output, int64_t count,
     if (grid < 0) {
         return fail(CUVIT_LENGTH_ERROR, "Elementwise launch exceeds the CUDA grid limit");
     }
-    convert_bf16_kernel<<<static_cast<unsigned>(grid), kThreads, 0,
-                          reinterpret_cast<cudaStream_t>(stream)>>>(
-        input, static_cast<__nv_bfloat16*>(output), count);
+    cuvit::host::pdl_launch(convert_bf16_kernel, static_cast<unsigned>(grid), kThreads, 0,
+                            reinterpret_cast<cudaStream_t>(stream), input,
+                            static_cast<__nv_bfloat16*>(output), count);
     return cuvit::host::after_launch("convert_f32_to_bf16");
 }
 
@@ -732,8 +761,8 @@ int cuvit_round_to_tf32(const float* input, float* output, int64_t count,
     if (grid < 0) {
         return fail(CUVIT_LENGTH_ERROR, "Elementwise launch exceeds the CUDA grid limit");
     }
-    round_tf32_kernel<<<static_cast<unsigned>(grid), kThreads, 0,
-                        reinterpret_cast<cudaStream_t>(stream)>>>(input, output, count);
+    cuvit::host::pdl_launch(round_tf32_kernel, static_cast<unsigned>(grid), kThreads, 0,
+                            reinterpret_cast<cudaStream_t>(stream), input, output, count);
     return cuvit::host::after_launch("round_to_tf32");
 }
 

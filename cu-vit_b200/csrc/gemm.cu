@@ -37,6 +37,8 @@ __global__ void __launch_bounds__(kSimtThreads)
                      int count, int inner, long long stride_a, long long stride_b,
                      long long stride_c, long long outer_a, long long outer_b, long long outer_c,
                      int accumulate, int apply_gelu) {
+    dev::grid_dependency_wait();
+    dev::grid_launch_dependents();
     __shared__ float tile_a[kSimtK][kSimtTile + 4];
     __shared__ float tile_b[kSimtK][kSimtTile + 4];
 
@@ -155,19 +157,21 @@ int launch_simt(const Resolved& r, cudaStream_t stream) {
     const int c_kind = r.c_dtype;
     const cuvit_gemm_batch& batch = p.batch;
     if (r.math == CUVIT_MATH_BF16) {
-        simt_gemm_kernel<__nv_bfloat16><<<grid, kSimtThreads, 0, stream>>>(
-            static_cast<const __nv_bfloat16*>(r.a), static_cast<const __nv_bfloat16*>(r.b),
-            r.bias, r.c, c_kind, p.m, p.n, p.k, p.alpha, r.transposed ? 1 : 0, r.lda, r.ldb,
-            r.ldc, batch.count, batch.inner, batch.stride_a, batch.stride_b, batch.stride_c,
-            batch.outer_stride_a, batch.outer_stride_b, batch.outer_stride_c,
-            p.epilogue.accumulate ? 1 : 0, p.epilogue.gelu ? 1 : 0);
+        host::pdl_launch(simt_gemm_kernel<__nv_bfloat16>, grid, kSimtThreads, 0, stream,
+                         static_cast<const __nv_bfloat16*>(r.a),
+                         static_cast<const __nv_bfloat16*>(r.b), r.bias, r.c, c_kind, p.m, p.n,
+                         p.k, p.alpha, r.transposed ? 1 : 0, r.lda, r.ldb, r.ldc, batch.count,
+                         batch.inner, batch.stride_a, batch.stride_b, batch.stride_c,
+                         batch.outer_stride_a, batch.outer_stride_b, batch.outer_stride_c,
+                         p.epilogue.accumulate ? 1 : 0, p.epilogue.gelu ? 1 : 0);
     } else {
-        simt_gemm_kernel<float><<<grid, kSimtThreads, 0, stream>>>(
-            static_cast<const float*>(r.a), static_cast<const float*>(r.b), r.bias, r.c, c_kind,
-            p.m, p.n, p.k, p.alpha, r.transposed ? 1 : 0, r.lda, r.ldb, r.ldc, batch.count,
-            batch.inner, batch.stride_a, batch.stride_b, batch.stride_c, batch.outer_stride_a,
-            batch.outer_stride_b, batch.outer_stride_c, p.epilogue.accumulate ? 1 : 0,
-            p.epilogue.gelu ? 1 : 0);
+        host::pdl_launch(simt_gemm_kernel<float>, grid, kSimtThreads, 0, stream,
+                         static_cast<const float*>(r.a), static_cast<const float*>(r.b), r.bias,
+                         r.c, c_kind, p.m, p.n, p.k, p.alpha, r.transposed ? 1 : 0, r.lda,
+                         r.ldb, r.ldc, batch.count, batch.inner, batch.stride_a, batch.stride_b,
+                         batch.stride_c, batch.outer_stride_a, batch.outer_stride_b,
+                         batch.outer_stride_c, p.epilogue.accumulate ? 1 : 0,
+                         p.epilogue.gelu ? 1 : 0);
     }
     return host::after_launch("simt_gemm_kernel");
 }

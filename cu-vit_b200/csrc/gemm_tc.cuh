@@ -364,6 +364,10 @@ __global__ void __launch_bounds__(TcShape<ElemBytes, BN, Split>::kThreads, 1)
     __syncthreads();
     dev::tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    // Inputs of this launch may come from the previous one: nothing global is read or
+    // written before it has finished.
+    dev::grid_dependency_wait();
+    dev::grid_launch_dependents();
 
     const int per_entry = p.m_tiles * p.n_tiles;
 

@@ -19,8 +19,8 @@ int launch_instance(const Plan& plan, cudaStream_t stream) {
             kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Shape::kSmemBytes);
     });
     CUVIT_TRY_CUDA(attribute_error);
-    kernel<<<plan.grid, Shape::kThreads, Shape::kSmemBytes, stream>>>(plan.map_a, plan.map_b,
-                                                                       plan.map_c, plan.params);
+    host::pdl_launch(kernel, plan.grid, Shape::kThreads, Shape::kSmemBytes, stream, plan.map_a,
+                     plan.map_b, plan.map_c, plan.params);
     return host::after_launch("tc_gemm_kernel");
 }
 

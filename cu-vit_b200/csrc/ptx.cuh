@@ -91,6 +91,21 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, unsigne
     }
 }
 
+// Programmatic dependent launch: kernels are launched so that they may start while the
+// previous kernel in the stream is still finishing. Each kernel runs its prologue (barrier
+// set-up, TMEM allocation, descriptor prefetch), then waits here until the previous grid has
+// completed and its writes are visible, before touching any data. Without the launch
+// attribute the wait returns at once.
+__device__ __forceinline__ void grid_dependency_wait() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
+// Lets the next kernel in the stream begin launching (its CTAs still wait for this grid to
+// complete before reading anything).
+__device__ __forceinline__ void grid_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // Makes generic-proxy shared-memory writes visible to the async proxy (TMA, tensor core).
 __device__ __forceinline__ void fence_proxy_async_shared() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");

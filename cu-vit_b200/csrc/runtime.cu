@@ -95,6 +95,14 @@ int current_context(const DeviceContext** context) {
 
 bool is_blackwell(const DeviceContext& context) { return context.major == 10; }
 
+bool pdl_enabled() {
+    static const bool enabled = []() {
+        const char* value = std::getenv("CUVIT_PDL");
+        return value != nullptr && std::strcmp(value, "1") == 0;
+    }();
+    return enabled;
+}
+
 int tensor_map_encoder(TensorMapEncodeFn* function) {
     static TensorMapEncodeFn cached = nullptr;
     static std::once_flag once;
