@@ -11,8 +11,11 @@ pass over one batch. Rank 0 prints one JSON line.
 
   value   images/s over all ranks, inputs resident in HBM, CUDA-graph replay, timed with CUDA
           events on the launching stream, max over ranks
-  e2e     the same through the public host-buffer call (VisionTransformer.forward_host: pinned
-          host images -> device, forward, logits -> host, synchronise) every step
+  e2e     the same through the public host-buffer call (VisionTransformer.forward_host_async,
+          the serving-loop form of forward_host): every step copies its pinned host images to
+          the device, runs the pass and copies the logits back to pinned host memory; the copy
+          of step i+1 overlaps the pass of step i, and the timed region ends when the last
+          step's logits are on the host
   roofline  the tcgen05 GEMMs (the dominant kernel): algorithmic FLOPs / device time of every
           GEMM launch, from CUDA events around each launch over profiled passes
   cpu_baseline  the reference's own CPU forward pass (oracle/_ref, compiled from its sources)
@@ -307,10 +310,10 @@ def our_arm(args) -> None:
     device_logits = torch.zeros_like(logits)
 
     def e2e_step():
-        model.forward_host_ptr(pinned_images.data_ptr(), pinned_logits.data_ptr(), batch,
-                               stream)
-        if world > 1:
-            device_logits.copy_(pinned_logits, non_blocking=False)
+        model.forward_host_async(pinned_images.data_ptr(), pinned_logits.data_ptr(), batch,
+                                 stream)
+        if world > 1:  # ordered after the logits' copy to the host on the same stream
+            device_logits.copy_(pinned_logits, non_blocking=True)
             gather_logits(device_logits, world, rank)
 
     for _ in range(args.warmup):

@@ -156,10 +156,24 @@ struct cuvit_vit {
     float* scores = nullptr; // FP32 path only: [B*h, T, score_ld]
     int score_ld = 0;
     float* stage_images = nullptr;
+    float* stage_images_alt = nullptr; // second image slot of forward_host_async
     float* stage_logits = nullptr;
 
     cudaStream_t capture_stream = nullptr;
     std::map<std::tuple<int, const float*, float*>, cudaGraphExec_t> graphs;
+
+    // forward_host: images per chunk (0 = automatic), the stream that carries the
+    // host-to-device copies, and one event per chunk marking its copy complete.
+    int host_chunk = 0;
+    cudaStream_t copy_stream = nullptr;
+    cudaEvent_t entry_event = nullptr;
+    std::vector<cudaEvent_t> chunk_events;
+
+    // forward_host_async: the image slot the next call fills, and per slot the events
+    // "its images have landed" and "the pass reading them has finished".
+    int async_slot = 0;
+    cudaEvent_t slot_loaded[2] = {nullptr, nullptr};
+    cudaEvent_t slot_free[2] = {nullptr, nullptr};
 };
 
 namespace cuvit::model {
@@ -533,6 +547,8 @@ int build(cuvit_vit* m, const float* const* host) {
         {&m->class_rows, static_cast<size_t>(images * e * ebytes)},
         {reinterpret_cast<void**>(&m->stage_images),
          static_cast<size_t>(images * c.channels * c.image_size * c.image_size * 4)},
+        {reinterpret_cast<void**>(&m->stage_images_alt),
+         static_cast<size_t>(images * c.channels * c.image_size * c.image_size * 4)},
         {reinterpret_cast<void**>(&m->stage_logits), static_cast<size_t>(images * c.classes * 4)},
     };
     if (m->precision == CUVIT_MATH_FP32) {
@@ -551,6 +567,12 @@ int build(cuvit_vit* m, const float* const* host) {
     }
     m->activation_used = activation_size;
     CUVIT_TRY_CUDA(cudaStreamCreateWithFlags(&m->capture_stream, cudaStreamNonBlocking));
+    CUVIT_TRY_CUDA(cudaStreamCreateWithFlags(&m->copy_stream, cudaStreamNonBlocking));
+    CUVIT_TRY_CUDA(cudaEventCreateWithFlags(&m->entry_event, cudaEventDisableTiming));
+    for (int slot = 0; slot < 2; ++slot) {
+        CUVIT_TRY_CUDA(cudaEventCreateWithFlags(&m->slot_loaded[slot], cudaEventDisableTiming));
+        CUVIT_TRY_CUDA(cudaEventCreateWithFlags(&m->slot_free[slot], cudaEventDisableTiming));
+    }
     return CUVIT_OK;
 }
 
@@ -559,6 +581,24 @@ void release(cuvit_vit* m) {
         cudaGraphExecDestroy(entry.second);
     }
     m->graphs.clear();
+    for (cudaEvent_t event : m->chunk_events) {
+        cudaEventDestroy(event);
+    }
+    m->chunk_events.clear();
+    if (m->entry_event != nullptr) {
+        cudaEventDestroy(m->entry_event);
+    }
+    for (int slot = 0; slot < 2; ++slot) {
+        if (m->slot_loaded[slot] != nullptr) {
+            cudaEventDestroy(m->slot_loaded[slot]);
+        }
+        if (m->slot_free[slot] != nullptr) {
+            cudaEventDestroy(m->slot_free[slot]);
+        }
+    }
+    if (m->copy_stream != nullptr) {
+        cudaStreamDestroy(m->copy_stream);
+    }
     if (m->capture_stream != nullptr) {
         cudaStreamDestroy(m->capture_stream);
     }
@@ -719,6 +759,51 @@ int create(const cuvit_vit_config* config, const float* const* tensors, int max_
     return CUVIT_OK;
 }
 
+// The executable graph of one whole pass for (batch, images, logits), captured on first use.
+// Work already queued on `stream` uses the same activation buffers, so the eager warm-up
+// pass and the capture start only after it.
+int graph_for(cuvit_vit& m, const float* images, float* logits, int batch, cudaStream_t stream,
+              cudaGraphExec_t* exec) {
+    const auto key = std::make_tuple(batch, images, logits);
+    auto found = m.graphs.find(key);
+    if (found == m.graphs.end()) {
+        CUVIT_TRY_CUDA(cudaEventRecord(m.entry_event, stream));
+        CUVIT_TRY_CUDA(cudaStreamWaitEvent(m.capture_stream, m.entry_event, 0));
+        // One eager pass first, so every one-time set-up (device context, kernel attributes,
+        // the driver's tensor-map entry point) happens outside the capture, where device
+        // synchronisation is allowed.
+        CUVIT_TRY(run_forward(m, images, logits, batch, m.capture_stream));
+        CUVIT_TRY_CUDA(cudaStreamSynchronize(m.capture_stream));
+        // Capture on the model's own stream: the caller's may be the legacy default stream,
+        // which cannot be captured.
+        CUVIT_TRY_CUDA(
+            cudaStreamBeginCapture(m.capture_stream, cudaStreamCaptureModeThreadLocal));
+        const int status = run_forward(m, images, logits, batch, m.capture_stream);
+        cudaGraph_t graph = nullptr;
+        const cudaError_t end = cudaStreamEndCapture(m.capture_stream, &graph);
+        CUVIT_TRY(status);
+        CUVIT_TRY_CUDA(end);
+        cudaGraphExec_t made = nullptr;
+        const cudaError_t instantiated = cudaGraphInstantiate(&made, graph, 0);
+        cudaGraphDestroy(graph);
+        CUVIT_TRY_CUDA(instantiated);
+        found = m.graphs.emplace(key, made).first;
+    }
+    *exec = found->second;
+    return CUVIT_OK;
+}
+
+// Images per forward_host chunk: halves from 64 images up, a single pass below that. The
+// second half's copy hides behind the first half's pass; finer chunks expose less copy time
+// but cost more in GEMM wave quantization than they save (ViT-B/16, B=256, on B200: halves
+// 12.97 ms, quarters 13.76 ms, one pass 13.56 ms).
+int host_chunk_images(const cuvit_vit& m, int batch) {
+    if (m.host_chunk > 0) {
+        return m.host_chunk < batch ? m.host_chunk : batch;
+    }
+    return batch >= 64 ? (batch + 1) / 2 : batch;
+}
+
 } // namespace
 } // namespace cuvit::model
 
@@ -860,16 +945,89 @@ int cuvit_vit_forward_host(cuvit_vit* model, const float* images, float* logits,
     DeviceGuard guard(model->device);
     const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
     const cuvit_vit_config& c = model->config;
-    const size_t image_bytes =
-        static_cast<size_t>(batch) * c.channels * c.image_size * c.image_size * sizeof(float);
+    const size_t per_image = static_cast<size_t>(c.channels) * c.image_size * c.image_size;
+    const int chunk = host_chunk_images(*model, batch);
+    const int chunks = (batch + chunk - 1) / chunk;
+
+    // Graphs for every chunk exist before the first copy is queued: a capture synchronizes
+    // the model's capture stream and must not sit between a copy and the pass that reads it.
+    std::vector<cudaGraphExec_t> execs(chunks);
+    for (int i = 0; i < chunks; ++i) {
+        const int images_here = i + 1 < chunks ? chunk : batch - i * chunk;
+        CUVIT_TRY(graph_for(*model, model->stage_images + static_cast<size_t>(i) * chunk *
+                                                              per_image,
+                            model->stage_logits + static_cast<size_t>(i) * chunk * c.classes,
+                            images_here, s, &execs[i]));
+    }
+    while (static_cast<int>(model->chunk_events.size()) < chunks) {
+        cudaEvent_t event = nullptr;
+        CUVIT_TRY_CUDA(cudaEventCreateWithFlags(&event, cudaEventDisableTiming));
+        model->chunk_events.push_back(event);
+    }
+
+    // Copies run on the copy stream, chunk after chunk, each pass on the caller's stream once
+    // its chunk has landed: chunk i+1 crosses PCIe while chunk i computes. Every chunk owns
+    // its slice of the staging buffer, so no copy overwrites images a pass still reads.
+    CUVIT_TRY_CUDA(cudaEventRecord(model->entry_event, s));
+    CUVIT_TRY_CUDA(cudaStreamWaitEvent(model->copy_stream, model->entry_event, 0));
+    for (int i = 0; i < chunks; ++i) {
+        const int images_here = i + 1 < chunks ? chunk : batch - i * chunk;
+        const size_t offset = static_cast<size_t>(i) * chunk * per_image;
+        CUVIT_TRY_CUDA(cudaMemcpyAsync(model->stage_images + offset, images + offset,
+                                       images_here * per_image * sizeof(float),
+                                       cudaMemcpyHostToDevice, model->copy_stream));
+        CUVIT_TRY_CUDA(cudaEventRecord(model->chunk_events[i], model->copy_stream));
+    }
+    for (int i = 0; i < chunks; ++i) {
+        CUVIT_TRY_CUDA(cudaStreamWaitEvent(s, model->chunk_events[i], 0));
+        CUVIT_TRY_CUDA(cudaGraphLaunch(execs[i], s));
+    }
     const size_t logit_bytes = static_cast<size_t>(batch) * c.classes * sizeof(float);
-    CUVIT_TRY_CUDA(
-        cudaMemcpyAsync(model->stage_images, images, image_bytes, cudaMemcpyHostToDevice, s));
-    CUVIT_TRY(cuvit_vit_forward_graph(model, model->stage_images, model->stage_logits, batch,
-                                      stream));
     CUVIT_TRY_CUDA(
         cudaMemcpyAsync(logits, model->stage_logits, logit_bytes, cudaMemcpyDeviceToHost, s));
     CUVIT_TRY_CUDA(cudaStreamSynchronize(s));
+    return CUVIT_OK;
+}
+
+int cuvit_vit_forward_host_async(cuvit_vit* model, const float* images, float* logits,
+                                 int batch, cuvit_stream_t stream) {
+    CUVIT_TRY(check_forward_args(model, images, logits, batch));
+    if (batch == 0) {
+        return CUVIT_OK;
+    }
+    DeviceGuard guard(model->device);
+    const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    const cuvit_vit_config& c = model->config;
+    const int slot = model->async_slot;
+    float* const staged = slot == 0 ? model->stage_images : model->stage_images_alt;
+    cudaGraphExec_t exec = nullptr;
+    CUVIT_TRY(graph_for(*model, staged, model->stage_logits, batch, s, &exec));
+    model->async_slot = slot ^ 1;
+    // The copy waits only for the pass that last read this slot (two calls back), so it
+    // overlaps the pass of the previous call; the pass waits for the copy.
+    const size_t image_bytes =
+        static_cast<size_t>(batch) * c.channels * c.image_size * c.image_size * sizeof(float);
+    CUVIT_TRY_CUDA(cudaStreamWaitEvent(model->copy_stream, model->slot_free[slot], 0));
+    CUVIT_TRY_CUDA(
+        cudaMemcpyAsync(staged, images, image_bytes, cudaMemcpyHostToDevice, model->copy_stream));
+    CUVIT_TRY_CUDA(cudaEventRecord(model->slot_loaded[slot], model->copy_stream));
+    CUVIT_TRY_CUDA(cudaStreamWaitEvent(s, model->slot_loaded[slot], 0));
+    CUVIT_TRY_CUDA(cudaGraphLaunch(exec, s));
+    CUVIT_TRY_CUDA(cudaEventRecord(model->slot_free[slot], s));
+    const size_t logit_bytes = static_cast<size_t>(batch) * c.classes * sizeof(float);
+    CUVIT_TRY_CUDA(
+        cudaMemcpyAsync(logits, model->stage_logits, logit_bytes, cudaMemcpyDeviceToHost, s));
+    return CUVIT_OK;
+}
+
+int cuvit_vit_set_host_chunk(cuvit_vit* model, int images) {
+    if (model == nullptr) {
+        return fail(CUVIT_INVALID_ARGUMENT, "model cannot be null");
+    }
+    if (images < 0) {
+        return fail(CUVIT_INVALID_ARGUMENT, "the host chunk size cannot be negative");
+    }
+    model->host_chunk = images;
     return CUVIT_OK;
 }
 
@@ -880,30 +1038,10 @@ int cuvit_vit_forward_graph(cuvit_vit* model, const float* images, float* logits
         return CUVIT_OK;
     }
     DeviceGuard guard(model->device);
-    const auto key = std::make_tuple(batch, images, logits);
-    auto found = model->graphs.find(key);
-    if (found == model->graphs.end()) {
-        // One eager pass first, so every one-time set-up (device context, kernel attributes,
-        // the driver's tensor-map entry point) happens outside the capture, where device
-        // synchronisation is allowed.
-        CUVIT_TRY(run_forward(*model, images, logits, batch, model->capture_stream));
-        CUVIT_TRY_CUDA(cudaStreamSynchronize(model->capture_stream));
-        // Capture on the model's own stream: the caller's may be the legacy default stream,
-        // which cannot be captured.
-        CUVIT_TRY_CUDA(cudaStreamBeginCapture(model->capture_stream,
-                                              cudaStreamCaptureModeThreadLocal));
-        const int status = run_forward(*model, images, logits, batch, model->capture_stream);
-        cudaGraph_t graph = nullptr;
-        const cudaError_t end = cudaStreamEndCapture(model->capture_stream, &graph);
-        CUVIT_TRY(status);
-        CUVIT_TRY_CUDA(end);
-        cudaGraphExec_t exec = nullptr;
-        const cudaError_t made = cudaGraphInstantiate(&exec, graph, 0);
-        cudaGraphDestroy(graph);
-        CUVIT_TRY_CUDA(made);
-        found = model->graphs.emplace(key, exec).first;
-    }
-    CUVIT_TRY_CUDA(cudaGraphLaunch(found->second, reinterpret_cast<cudaStream_t>(stream)));
+    const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    cudaGraphExec_t exec = nullptr;
+    CUVIT_TRY(graph_for(*model, images, logits, batch, s, &exec));
+    CUVIT_TRY_CUDA(cudaGraphLaunch(exec, s));
     return CUVIT_OK;
 }
 

@@ -140,6 +140,8 @@ SIGNATURES = {
     "cuvit_vit_destroy": (_i, [_vp]),
     "cuvit_vit_forward": (_i, [_vp, _vp, _vp, _i, _vp]),
     "cuvit_vit_forward_host": (_i, [_vp, _vp, _vp, _i, _vp]),
+    "cuvit_vit_forward_host_async": (_i, [_vp, _vp, _vp, _i, _vp]),
+    "cuvit_vit_set_host_chunk": (_i, [_vp, _i]),
     "cuvit_vit_forward_graph": (_i, [_vp, _vp, _vp, _i, _vp]),
     "cuvit_vit_forward_profiled": (
         _i, [_vp, _vp, _vp, _i, _vp, ctypes.POINTER(LaunchRecordC), _i, ctypes.POINTER(_i)]

@@ -210,6 +210,19 @@ class VisionTransformer:
                                                     ctypes.c_void_p(logits_ptr), batch,
                                                     _stream(stream)))
 
+    def forward_host_async(self, images_ptr: int, logits_ptr: int, batch: int,
+                           stream=None) -> None:
+        """Queues copy-in, pass and copy-out on caller-owned pinned host buffers and returns;
+        the copy of the next call overlaps this call's pass. Results are valid once `stream`
+        has been synchronised."""
+        check(_lib.library().cuvit_vit_forward_host_async(
+            self._handle, ctypes.c_void_p(images_ptr), ctypes.c_void_p(logits_ptr), batch,
+            _stream(stream)))
+
+    def set_host_chunk(self, images: int) -> None:
+        """Images per forward_host() chunk (copy of chunk i+1 overlaps chunk i); 0 = automatic."""
+        check(_lib.library().cuvit_vit_set_host_chunk(self._handle, images))
+
     def forward_profiled(self, images, logits, batch: int, stream=None) -> list[dict]:
         """forward() with CUDA events around every launch; returns one record per launch:
         kind, layer, algorithmic flops and bytes, and device milliseconds."""

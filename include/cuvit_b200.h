@@ -282,9 +282,25 @@ int cuvit_vit_forward(cuvit_vit* model, const float* images, float* logits, int 
                       cuvit_stream_t stream);
 /* Host-memory convenience (reference: forward(std::vector), vit.cu:319-344): copies host
  * images in, runs, copies logits out and synchronizes. Uses staging buffers allocated at
- * creation, so it allocates nothing per call; pinned host memory copies asynchronously. */
+ * creation, so it allocates nothing per call. Batches of 64 images and more run in two
+ * halves: the second half's copy runs on a second stream while the first half computes,
+ * which needs pinned host memory to overlap. Logits do not depend on the chunking (every
+ * image's result is independent of the batch it runs in). */
 int cuvit_vit_forward_host(cuvit_vit* model, const float* images, float* logits, int batch,
                            cuvit_stream_t stream);
+/* forward_host() without the final synchronisation, for serving loops: queues the copy of
+ * the images into one of two staging slots (on a second stream), the pass on `stream`, and
+ * the copy of the logits back to `logits`, then returns. The copy of call i+1 overlaps the
+ * pass of call i. The host buffers must stay valid and unchanged until `stream` has reached
+ * this call's work (synchronize it, or wait on an event recorded after the call); the images
+ * must hold their data when the call is made, since the copy is not ordered after earlier
+ * work on `stream`. Consecutive calls on one model must use the same stream. No reference
+ * counterpart (the reference's host-vector forward is synchronous). */
+int cuvit_vit_forward_host_async(cuvit_vit* model, const float* images, float* logits,
+                                 int batch, cuvit_stream_t stream);
+/* Images per forward_host chunk; 0 restores the automatic choice. No reference
+ * counterpart (the reference copies the whole batch before running it). */
+int cuvit_vit_set_host_chunk(cuvit_vit* model, int images);
 /* Replays a CUDA graph of the whole pass for this batch size (captured on first use). */
 int cuvit_vit_forward_graph(cuvit_vit* model, const float* images, float* logits, int batch,
                             cuvit_stream_t stream);

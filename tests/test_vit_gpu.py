@@ -103,6 +103,73 @@ def test_partial_batch_is_clean_and_graph_matches_eager(cuda):
     np.testing.assert_array_equal(host, full)
 
 
+def test_chunked_host_path_matches_eager(cuda):
+    """forward_host() runs the batch in chunks whose copies overlap the previous chunk's
+    pass; every chunking (automatic, ragged, larger than the batch, pinned or pageable host
+    memory) gives the eager logits bitwise."""
+    _, config, _, std, _, _ = golden_case("vit hd64")
+    weights = random_weights(config, 717, std=std)
+    batch = 40
+    model = VisionTransformer(config, weights, max_batch=batch, precision=PRECISION_BF16)
+    images = mg.vit_images(config, batch, 31)
+    eager = model_logits(model, images, batch, cuda)
+    np.testing.assert_array_equal(model.forward_host(images), eager)  # automatic: one pass
+    for chunk in (3, 7, 64, 0):
+        model.set_host_chunk(chunk)
+        np.testing.assert_array_equal(model.forward_host(images), eager, err_msg=str(chunk))
+        np.testing.assert_array_equal(model.forward_host(images[:7 * config.image_elements()]),
+                                      eager[:7], err_msg=f"{chunk} partial")
+    model.set_host_chunk(9)
+    pinned_images = cuda.from_numpy(images).pin_memory()
+    pinned_logits = cuda.zeros(batch, config.classes).pin_memory()
+    model.forward_host_ptr(pinned_images.data_ptr(), pinned_logits.data_ptr(), batch)
+    np.testing.assert_array_equal(pinned_logits.numpy(), eager)
+    with pytest.raises(InvalidArgument):
+        model.set_host_chunk(-1)
+    model.close()
+
+
+def test_async_host_calls_pipeline_correctly(cuda):
+    """forward_host_async(): back-to-back calls on alternating staging slots, with batch
+    sizes that change between calls, each give the eager logits of their own images."""
+    _, config, _, std, _, _ = golden_case("vit hd64")
+    weights = random_weights(config, 737, std=std)
+    model = VisionTransformer(config, weights, max_batch=6, precision=PRECISION_BF16)
+    per_image = config.image_elements()
+    batches = [6, 6, 3, 6, 1, 5, 6]
+    inputs = [mg.vit_images(config, b, 50 + i) for i, b in enumerate(batches)]
+    want = [model_logits(model, x, b, cuda) for x, b in zip(inputs, batches)]
+    pinned_in = [cuda.from_numpy(x).pin_memory() for x in inputs]
+    pinned_out = [cuda.full((b, config.classes), float("nan")).pin_memory() for b in batches]
+    stream = cuda.cuda.current_stream()
+    for x, out, b in zip(pinned_in, pinned_out, batches):
+        model.forward_host_async(x.data_ptr(), out.data_ptr(), b, stream)
+    stream.synchronize()
+    for i, (out, w) in enumerate(zip(pinned_out, want)):
+        np.testing.assert_array_equal(out.numpy(), w, err_msg=f"call {i}")
+    assert per_image * 6 == pinned_in[0].numel()
+    # The synchronous path after asynchronous calls still sees its own images.
+    np.testing.assert_array_equal(model.forward_host(inputs[2]), want[2])
+    model.close()
+
+
+def test_graph_capture_waits_for_queued_work(cuda):
+    """A first forward_graph() for new buffers (eager warm-up + capture on the model's own
+    stream) queued behind an unfinished pass on the caller's stream must not disturb it."""
+    _, config, _, std, _, _ = golden_case("vit hd64")
+    weights = random_weights(config, 727, std=std)
+    model = VisionTransformer(config, weights, max_batch=4, precision=PRECISION_BF16)
+    images = [to_device(mg.vit_images(config, 4, seed)) for seed in (41, 42, 43)]
+    want = [model_logits(model, to_host(x), 4, cuda) for x in images]
+    outs = [cuda.full((4, config.classes), float("nan"), device="cuda") for _ in images]
+    for x, out in zip(images, outs):  # no synchronisation between the calls
+        model.forward_graph(x, out, 4)
+    cuda.cuda.synchronize()
+    for out, w in zip(outs, want):
+        np.testing.assert_array_equal(to_host(out), w)
+    model.close()
+
+
 def test_limits_and_memory(cuda):
     _, config, _, std, _, _ = golden_case("vit small")
     weights = random_weights(config, 808, std=std)
