@@ -318,15 +318,23 @@ __global__ void __launch_bounds__(kThreads)
 // ---------------------------------------------------------------------------------------
 // BF16: persistent, pipelined variant. One CTA per SM walks (image, head) pairs; Q, K, V of
 // the next pair load into the second of two shared-memory buffers while the current pair is
-// in softmax. Each 128-row query tile has its own softmax warpgroup and its own 256-column
-// TMEM region (S, then P packed in its first half, then O at +128), so both tiles run at
-// once. The context is written through per-warp shared-memory slabs by TMA stores.
+// in softmax. Each 128-row query tile has its own 256-column TMEM region and two softmax
+// warpgroups that split its key columns at `split` (a multiple of 32). The row extreme and
+// the row sum are combined through shared memory; each warpgroup writes its packed bf16 P
+// into the first half of its own score columns, so neither overwrites scores the other still
+// reads: keys below `split` land at column key/2, the rest at split + (key - split)/2. O then
+// accumulates into 64 columns that neither P occupies (`o_col`). Each softmax warp writes 32
+// context rows x 32 features through a shared-memory slab by TMA store.
 //
-// Roles: warp 0 TMA loads, warp 1 MMA issue, warp 2 TMEM, warps 4..7 softmax of query tile
-// 0, warps 8..11 of query tile 1.
+// Roles: warp 0 TMA loads, warps 1 and 3 MMA issue for query tiles 0 and 1, warp 2 TMEM;
+// softmax warp w (4..19) has query tile ((w - 4) >> 2) & 1, key half (w - 4) >> 3 and TMEM
+// lane quarter w & 3, so every SM sub-partition runs one warp of each (tile, half).
 // ---------------------------------------------------------------------------------------
-constexpr int kPipeThreads = 384;
-constexpr int kPipeSlabBytes = 32 * 128; // one warp's 32 context rows x 128 bytes
+constexpr int kPipeThreads = 640;
+constexpr int kPipeSoftmaxWarps = 16;
+constexpr int kPipeSlabBytes = 32 * 64; // one warp's 32 context rows x 32 bf16 features
+constexpr int kPipeExchangeBytes = 2 * 2 * 2 * kTileQ * 4; // {extreme, sum} x tile x half x row
+constexpr int kPipeBarriers = 14;
 
 struct PipeParams {
     int tokens;
@@ -335,10 +343,18 @@ struct PipeParams {
     int q_tiles;
     int pairs;        // batch * heads
     int buffer_bytes; // one Q/K/V buffer, 1024-aligned
+    int split;        // first key column of the second softmax warpgroup
+    int o_col;        // first TMEM column of O within a tile's region
     float scale;
     float scale_log2;
     unsigned* status;
 };
+
+// Shared memory of the pipelined kernel for one Q/K/V buffer size.
+constexpr int pipe_smem_bytes(int buffer_bytes) {
+    return 1024 + 2 * buffer_bytes + kPipeSoftmaxWarps * kPipeSlabBytes + kPipeExchangeBytes +
+           8 * kPipeBarriers + 16;
+}
 
 __global__ void __launch_bounds__(kPipeThreads, 1)
     attention_bf16_pipelined(const __grid_constant__ CUtensorMap map_q,
@@ -358,13 +374,16 @@ __global__ void __launch_bounds__(kPipeThreads, 1)
     };
     const auto v_smem = [&](int b) -> uint32_t { return k_smem(b) + kv_region; };
     const int slab_offset = 2 * p.buffer_bytes;
-    const uint32_t bar_base = base + slab_offset + 8 * kPipeSlabBytes;
-    // barriers: buf_full[2], buf_empty[2], s_full[2], p_full[2], o_full[2], o_free[2], drain
+    const int exchange_offset = slab_offset + kPipeSoftmaxWarps * kPipeSlabBytes;
+    const uint32_t bar_base = base + exchange_offset + kPipeExchangeBytes;
+    // barriers: buf_full[2], buf_empty[2], s_full[2], p_full[2], o_full[2], o_free[2],
+    // drain[2] (one per MMA issuer)
     const auto bar = [&](int kind, int i) -> uint32_t { return bar_base + 8u * (2 * kind + i); };
     constexpr int kBufFull = 0, kBufEmpty = 1, kSFull = 2, kPFull = 3, kOFull = 4, kOFree = 5;
-    const uint32_t bar_drain = bar_base + 8u * 12;
-    uint32_t* const tmem_slot =
-        reinterpret_cast<uint32_t*>(smem + slab_offset + 8 * kPipeSlabBytes + 8 * 13);
+    const uint32_t bar_drain0 = bar_base + 8u * 12;
+    const uint32_t bar_drain1 = bar_base + 8u * 13;
+    uint32_t* const tmem_slot = reinterpret_cast<uint32_t*>(
+        smem + exchange_offset + kPipeExchangeBytes + 8 * kPipeBarriers);
 
     const int warp = threadIdx.x / 32;
     const int lane = threadIdx.x % 32;
@@ -372,13 +391,14 @@ __global__ void __launch_bounds__(kPipeThreads, 1)
     if (threadIdx.x == 0) {
         for (int i = 0; i < 2; ++i) {
             dev::mbar_init(bar(kBufFull, i), 1);
-            dev::mbar_init(bar(kBufEmpty, i), 1);
+            dev::mbar_init(bar(kBufEmpty, i), static_cast<uint32_t>(p.q_tiles));
             dev::mbar_init(bar(kSFull, i), 1);
-            dev::mbar_init(bar(kPFull, i), 128);
+            dev::mbar_init(bar(kPFull, i), 256);
             dev::mbar_init(bar(kOFull, i), 1);
-            dev::mbar_init(bar(kOFree, i), 128);
+            dev::mbar_init(bar(kOFree, i), 256);
         }
-        dev::mbar_init(bar_drain, 1);
+        dev::mbar_init(bar_drain0, 1);
+        dev::mbar_init(bar_drain1, 1);
         dev::fence_barrier_init();
     }
     if (warp == 2) {
@@ -420,75 +440,96 @@ __global__ void __launch_bounds__(kPipeThreads, 1)
             const int cv[3] = {2 * hd + head * kHeadDim, 0, image};
             dev::tma_load(v_smem(b), &map_kv, bar(kBufFull, b), 3, cv);
         }
-    } else if (warp == 1 && lane == 0) {
-        // ---------------- MMA issue ----------------
+    } else if ((warp == 1 || (warp == 3 && p.q_tiles > 1)) && lane == 0) {
+        // ---------------- MMA issue: warp 1 for query tile 0, warp 3 for tile 1 ----------------
+        // Separate issuers let one tile's MMAs run while the other tile is in softmax, and
+        // each commit tracks only its own thread's MMAs.
+        const int t = warp == 1 ? 0 : 1;
         const uint32_t idesc_s = dev::make_idesc(1u, kTileQ, p.n_keys, false, false);
         constexpr uint32_t kIdescO = dev::make_idesc(1u, kTileQ, kHeadDim, false, true);
+        const int steps = p.n_keys / 16;
+        const int split_step = p.split / 16;
+        // 16 keys per PV MMA: V advances 16 rows (2048 bytes); P sits at column key/2 below
+        // the split and at split/2 + key/2 from it.
+        const uint32_t region = tmem + static_cast<uint32_t>(256 * t);
+        const uint32_t d_tmem = region + static_cast<uint32_t>(p.o_col);
+        const uint32_t a_high = region + static_cast<uint32_t>(p.split / 2);
+        const uint32_t bar_drain = t == 0 ? bar_drain0 : bar_drain1;
         bool ok = true;
         int i = 0;
         for (int pair = blockIdx.x; pair < p.pairs && ok; pair += gridDim.x, ++i) {
             const int b = i & 1;
             const uint32_t use = static_cast<uint32_t>(i >> 1);
             const uint32_t parity = static_cast<uint32_t>(i & 1);
-            if (!dev::mbar_wait(bar(kBufFull, b), use & 1u, p.status)) {
+            // The buffer's loads have landed and the previous pair's O_t has been read out of
+            // this TMEM region.
+            if (!dev::mbar_wait(bar(kBufFull, b), use & 1u, p.status) ||
+                !dev::mbar_wait(bar(kOFree, t), parity ^ 1u, p.status)) {
                 ok = false;
                 break;
             }
-            for (int t = 0; t < p.q_tiles && ok; ++t) {
-                // The previous pair's O_t must have been read out of this TMEM region.
-                if (!dev::mbar_wait(bar(kOFree, t), parity ^ 1u, p.status)) {
-                    ok = false;
-                    break;
-                }
-                dev::tc_fence_after();
-                const uint32_t s_tmem = tmem + static_cast<uint32_t>(256 * t);
+            dev::tc_fence_after();
+            // Descriptors are built once and stepped by adding to their start-address field
+            // (16-byte units): 32 bytes per K step.
+            const uint64_t q_desc = dev::smem_desc_sw128(q_smem(b, t), 16, 1024);
+            const uint64_t k_desc = dev::smem_desc_sw128(k_smem(b), 16, 1024);
 #pragma unroll
-                for (int kk = 0; kk < kHeadDim / 16; ++kk) {
-                    const uint64_t a_desc =
-                        dev::smem_desc_sw128(q_smem(b, t) + kk * 32, 16, 1024);
-                    const uint64_t b_desc = dev::smem_desc_sw128(k_smem(b) + kk * 32, 16, 1024);
-                    dev::mma_ss<dev::MmaKind::kF16>(s_tmem, a_desc, b_desc, idesc_s,
+            for (int kk = 0; kk < kHeadDim / 16; ++kk) {
+                dev::mma_ss<dev::MmaKind::kF16>(region, q_desc + 2 * kk, k_desc + 2 * kk,
+                                                idesc_s, kk > 0 ? 1u : 0u);
+            }
+            dev::tc_commit(bar(kSFull, t));
+            if (!dev::mbar_wait(bar(kPFull, t), parity, p.status)) {
+                ok = false;
+                break;
+            }
+            dev::tc_fence_after();
+            const uint64_t v_desc = dev::smem_desc_sw128(v_smem(b), kv_region, 1024);
+#pragma unroll
+            for (int kk = 0; kk < kMaxTokens / 16; ++kk) {
+                if (kk < steps) {
+                    const uint32_t a_tmem = (kk < split_step ? region : a_high) + 8u * kk;
+                    dev::mma_ts<dev::MmaKind::kF16>(d_tmem, a_tmem, v_desc + 128 * kk, kIdescO,
                                                     kk > 0 ? 1u : 0u);
                 }
-                dev::tc_commit(bar(kSFull, t));
             }
-            for (int t = 0; t < p.q_tiles && ok; ++t) {
-                if (!dev::mbar_wait(bar(kPFull, t), parity, p.status)) {
-                    ok = false;
-                    break;
-                }
-                dev::tc_fence_after();
-                const uint32_t region = tmem + static_cast<uint32_t>(256 * t);
-                const int steps = p.n_keys / 16;
-                for (int kk = 0; kk < steps; ++kk) {
-                    const uint64_t b_desc =
-                        dev::smem_desc_sw128(v_smem(b) + kk * 16 * 128, kv_region, 1024);
-                    dev::mma_ts<dev::MmaKind::kF16>(region + 128, region + kk * 8, b_desc,
-                                                    kIdescO, kk > 0 ? 1u : 0u);
-                }
-                dev::tc_commit(bar(kOFull, t));
-            }
-            if (ok) {
-                dev::tc_commit(bar(kBufEmpty, b)); // both tiles' MMAs have read buffer b
-            }
+            dev::tc_commit(bar(kOFull, t));
+            dev::tc_commit(bar(kBufEmpty, b)); // one arrival per tile
         }
         if (!ok) {
             dev::tc_commit(bar_drain);
             dev::mbar_wait(bar_drain, 0, p.status);
         }
     } else if (warp >= 4) {
-        // ---------------- softmax and output, one warpgroup per query tile ----------------
-        const int t = (warp - 4) >> 2;
+        // ---------------- softmax and output ----------------
+        const int sw = warp - 4;
+        const int t = (sw >> 2) & 1;
+        const int h = sw >> 3;
         const int quarter = warp & 3;
         const int row = quarter * 32 + lane;
         const uint32_t lane_field = static_cast<uint32_t>(quarter * 32) << 16;
         const uint32_t region = tmem + lane_field + static_cast<uint32_t>(256 * t);
-        uint8_t* const slab = smem + slab_offset + (warp - 4) * kPipeSlabBytes;
-        const uint32_t slab_addr = base + slab_offset + (warp - 4) * kPipeSlabBytes;
+        uint8_t* const slab = smem + slab_offset + sw * kPipeSlabBytes;
+        const uint32_t slab_addr = base + slab_offset + sw * kPipeSlabBytes;
+        // Exchange: extreme[t][half][row], then sum[t][half][row].
+        float* const x_extreme =
+            reinterpret_cast<float*>(smem + exchange_offset) + t * 2 * kTileQ;
+        float* const x_sum = x_extreme + 2 * 2 * kTileQ;
+        const uint32_t partner_barrier = 1u + static_cast<uint32_t>(t * 4 + quarter);
+        // This warp's 32-column score chunks [c_begin, c_end) and where its P goes.
+        const int chunks_all = (p.n_keys + 31) / 32;
+        const int c_begin = h == 0 ? 0 : p.split / 32;
+        const int c_end = h == 0 ? (p.split / 32 < chunks_all ? p.split / 32 : chunks_all)
+                                 : chunks_all;
+        const uint32_t p_base = h == 0 ? 0u : static_cast<uint32_t>(p.split);
         if (t < p.q_tiles) {
             if (lane == 0) {
                 dev::tma_prefetch_descriptor(&map_ctx);
             }
+            // A warp whose 32 query rows all lie past the token count has nothing to compute
+            // (both halves of a row quarter agree): its O rows would be clipped by the store.
+            const bool live = t * kTileQ + quarter * 32 < p.tokens;
+            const bool positive = p.scale >= 0.0F;
             int i = 0;
             for (int pair = blockIdx.x; pair < p.pairs; pair += gridDim.x, ++i) {
                 const uint32_t parity = static_cast<uint32_t>(i & 1);
@@ -496,62 +537,74 @@ __global__ void __launch_bounds__(kPipeThreads, 1)
                     break;
                 }
                 dev::tc_fence_after();
-                // A warp whose 32 query rows all lie past the token count has nothing to
-                // compute: its O rows are clipped by the context store.
-                const bool live = t * kTileQ + quarter * 32 < p.tokens;
                 float sum = 1.0F;
                 if (live) {
-                    // Two 32-column TMEM loads in flight per wait; chunk indices are
-                    // compile-time (the region is 256 columns wide), so the loaded values stay
-                    // in registers. Columns at or past n_keys are masked like padded keys.
                     // The row extreme of the raw scores: the maximum for a positive scale, the
-                    // minimum for a negative one; scale is applied once, to the extreme.
-                    const bool positive = p.scale >= 0.0F;
-                    float extreme = positive ? -INFINITY : INFINITY;
+                    // minimum for a negative one; scale is applied once, to the extreme. Four
+                    // independent accumulators keep the dependency chains short.
+                    float ext[4];
+#pragma unroll
+                    for (int a = 0; a < 4; ++a) {
+                        ext[a] = positive ? -INFINITY : INFINITY;
+                    }
                     const auto reduce = [&](const uint32_t(&s)[32], int c) {
                         if ((c + 1) * 32 <= p.tokens) { // whole chunk of real keys
 #pragma unroll
                             for (int j = 0; j < 32; ++j) {
-                                extreme = positive ? fmaxf(extreme, __uint_as_float(s[j]))
-                                                   : fminf(extreme, __uint_as_float(s[j]));
+                                const float v = __uint_as_float(s[j]);
+                                ext[j & 3] = positive ? fmaxf(ext[j & 3], v) : fminf(ext[j & 3], v);
                             }
                         } else {
 #pragma unroll
                             for (int j = 0; j < 32; ++j) {
                                 if (c * 32 + j < p.tokens) {
-                                    extreme = positive ? fmaxf(extreme, __uint_as_float(s[j]))
-                                                       : fminf(extreme, __uint_as_float(s[j]));
+                                    const float v = __uint_as_float(s[j]);
+                                    ext[j & 3] =
+                                        positive ? fmaxf(ext[j & 3], v) : fminf(ext[j & 3], v);
                                 }
                             }
                         }
                     };
+                    // One 32-column TMEM load per wait (the other warps of the sub-partition
+                    // cover its latency); chunk indices relative to c_begin are compile-time,
+                    // so the loaded values stay in registers.
 #pragma unroll
-                    for (int c = 0; c < 8; c += 2) {
-                        if (c * 32 >= p.n_keys) {
+                    for (int r = 0; r < 8; ++r) {
+                        const int c = c_begin + r;
+                        if (c >= c_end) {
                             break;
                         }
                         uint32_t s0[32];
-                        uint32_t s1[32];
                         dev::tmem_load_32(region + c * 32, s0);
-                        dev::tmem_load_32(region + (c + 1) * 32, s1);
                         dev::tmem_wait_load();
                         reduce(s0, c);
-                        reduce(s1, c + 1);
                     }
+                    float extreme = positive ? fmaxf(fmaxf(ext[0], ext[1]), fmaxf(ext[2], ext[3]))
+                                             : fminf(fminf(ext[0], ext[1]), fminf(ext[2], ext[3]));
+                    x_extreme[h * kTileQ + row] = extreme;
+                    dev::named_barrier_sync(partner_barrier, 64);
+                    const float other = x_extreme[(h ^ 1) * kTileQ + row];
+                    extreme = positive ? fmaxf(extreme, other) : fminf(extreme, other);
                     const float offset = extreme * p.scale_log2;
-                    sum = 0.0F;
                     // P = exp(scale * s - max), packed to bf16 pairs in place; the row sum is
                     // taken over the FP32 values.
-                    const auto exp_pack = [&](const uint32_t(&s)[32], int c) {
+                    float sums[4] = {0.0F, 0.0F, 0.0F, 0.0F};
+                    const auto exp_pack = [&](const uint32_t(&s)[32], int c, uint32_t column) {
                         uint32_t packed[16];
                         if ((c + 1) * 32 <= p.tokens) {
+                            // One key pair in four takes 2^x on the FMA pipe, the rest on
+                            // the special-function unit, which would otherwise bound the pass.
 #pragma unroll
                             for (int j = 0; j < 16; ++j) {
-                                const float e0 = dev::ex2_approx(
-                                    fmaf(__uint_as_float(s[2 * j]), p.scale_log2, -offset));
-                                const float e1 = dev::ex2_approx(
-                                    fmaf(__uint_as_float(s[2 * j + 1]), p.scale_log2, -offset));
-                                sum += e0 + e1;
+                                const float x0 =
+                                    fmaf(__uint_as_float(s[2 * j]), p.scale_log2, -offset);
+                                const float x1 =
+                                    fmaf(__uint_as_float(s[2 * j + 1]), p.scale_log2, -offset);
+                                const float e0 =
+                                    (j & 3) == 3 ? dev::exp2_poly(x0) : dev::ex2_approx(x0);
+                                const float e1 =
+                                    (j & 3) == 3 ? dev::exp2_poly(x1) : dev::ex2_approx(x1);
+                                sums[j & 3] += e0 + e1;
                                 packed[j] = dev::pack_bf16x2(e0, e1);
                             }
                         } else {
@@ -568,26 +621,28 @@ __global__ void __launch_bounds__(kPipeThreads, 1)
                                     e1 = dev::ex2_approx(fmaf(__uint_as_float(s[2 * j + 1]),
                                                               p.scale_log2, -offset));
                                 }
-                                sum += e0 + e1;
+                                sums[j & 3] += e0 + e1;
                                 packed[j] = dev::pack_bf16x2(e0, e1);
                             }
                         }
-                        dev::tmem_store_16(region + c * 16, packed);
+                        dev::tmem_store_16(region + column, packed);
                     };
 #pragma unroll
-                    for (int c = 0; c < 8; c += 2) {
-                        if (c * 32 >= p.n_keys) {
+                    for (int r = 0; r < 8; ++r) {
+                        const int c = c_begin + r;
+                        if (c >= c_end) {
                             break;
                         }
                         uint32_t s0[32];
-                        uint32_t s1[32];
                         dev::tmem_load_32(region + c * 32, s0);
-                        dev::tmem_load_32(region + (c + 1) * 32, s1);
                         dev::tmem_wait_load();
-                        exp_pack(s0, c);
-                        exp_pack(s1, c + 1);
+                        exp_pack(s0, c, p_base + 16u * r);
                     }
+                    const float partial = (sums[0] + sums[1]) + (sums[2] + sums[3]);
+                    x_sum[h * kTileQ + row] = partial;
                     dev::tmem_wait_store();
+                    dev::named_barrier_sync(partner_barrier, 64);
+                    sum = partial + x_sum[(h ^ 1) * kTileQ + row];
                 }
                 dev::tc_fence_before();
                 dev::mbar_arrive(bar(kPFull, t));
@@ -595,43 +650,45 @@ __global__ void __launch_bounds__(kPipeThreads, 1)
                     break;
                 }
                 dev::tc_fence_after();
-                uint32_t o0[32];
-                uint32_t o1[32];
-                dev::tmem_load_32(region + 128, o0);
-                dev::tmem_load_32(region + 160, o1);
+                uint32_t o[32];
+                dev::tmem_load_32(region + static_cast<uint32_t>(p.o_col + 32 * h), o);
                 dev::tmem_wait_load();
                 dev::tc_fence_before();
                 dev::mbar_arrive(bar(kOFree, t)); // this TMEM region may take the next S
+                if (!live) {
+                    continue;
+                }
                 const float inverse = 1.0F / sum;
                 if (lane == 0) {
                     dev::bulk_wait_group_read0(); // the slab's previous store has been read
                 }
                 __syncwarp();
-                uint4* const slab_row = reinterpret_cast<uint4*>(slab + lane * 128);
+                // 64-byte rows with the 64-byte swizzle of the context tensor map: 16-byte
+                // chunk j of row r sits at chunk j ^ ((r >> 1) & 3).
+                uint4* const slab_row = reinterpret_cast<uint4*>(slab + lane * 64);
+                const int swizzle = (lane >> 1) & 3;
 #pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    const uint32_t* const o = j < 4 ? o0 : o1;
-                    const int base_j = (j & 3) * 8;
-                    slab_row[j ^ (lane & 7)] = make_uint4(
-                        dev::pack_bf16x2(__uint_as_float(o[base_j]) * inverse,
-                                         __uint_as_float(o[base_j + 1]) * inverse),
-                        dev::pack_bf16x2(__uint_as_float(o[base_j + 2]) * inverse,
-                                         __uint_as_float(o[base_j + 3]) * inverse),
-                        dev::pack_bf16x2(__uint_as_float(o[base_j + 4]) * inverse,
-                                         __uint_as_float(o[base_j + 5]) * inverse),
-                        dev::pack_bf16x2(__uint_as_float(o[base_j + 6]) * inverse,
-                                         __uint_as_float(o[base_j + 7]) * inverse));
+                for (int j = 0; j < 4; ++j) {
+                    slab_row[j ^ swizzle] = make_uint4(
+                        dev::pack_bf16x2(__uint_as_float(o[8 * j]) * inverse,
+                                         __uint_as_float(o[8 * j + 1]) * inverse),
+                        dev::pack_bf16x2(__uint_as_float(o[8 * j + 2]) * inverse,
+                                         __uint_as_float(o[8 * j + 3]) * inverse),
+                        dev::pack_bf16x2(__uint_as_float(o[8 * j + 4]) * inverse,
+                                         __uint_as_float(o[8 * j + 5]) * inverse),
+                        dev::pack_bf16x2(__uint_as_float(o[8 * j + 6]) * inverse,
+                                         __uint_as_float(o[8 * j + 7]) * inverse));
                 }
                 dev::fence_proxy_async_shared();
                 __syncwarp();
                 if (lane == 0) {
                     const int image = pair / p.heads;
                     const int head = pair - image * p.heads;
-                    const int coords[3] = {head * kHeadDim, t * kTileQ + quarter * 32, image};
+                    const int coords[3] = {head * kHeadDim + 32 * h,
+                                           t * kTileQ + quarter * 32, image};
                     dev::tma_store<false>(&map_ctx, slab_addr, 3, coords);
                     dev::bulk_commit_group();
                 }
-                (void)row;
             }
             if (lane == 0) {
                 dev::bulk_wait_group0();
@@ -646,12 +703,57 @@ __global__ void __launch_bounds__(kPipeThreads, 1)
     }
 }
 
+// Where the second softmax warpgroup's keys begin and where O accumulates, for n_keys score
+// columns: the split (a multiple of 32) that balances the two warpgroups' chunk counts, then
+// their real keys, among those that leave 64 TMEM columns free of both P halves. A split at
+// the rounded end gives the whole row to the first warpgroup. Returns false if none fits.
+bool choose_split(int tokens, int n_keys, int* split, int* o_col) {
+    const int end = (n_keys + 31) / 32 * 32;
+    const auto place_o = [&](int s) {
+        const int first = (s / 2 + 31) / 32 * 32; // free columns [s/2, s) of the first half
+        if (first + 64 <= s) {
+            return first;
+        }
+        const int second = (s + (end - s) / 2 + 31) / 32 * 32; // past the second P half
+        return second + 64 <= 256 ? second : -1;
+    };
+    int best_cost = 1 << 30;
+    for (int s = 32; s <= end; s += 32) {
+        const int o = place_o(s);
+        if (o < 0) {
+            continue;
+        }
+        const int chunks = s / 32 > (end - s) / 32 ? s / 32 : (end - s) / 32;
+        const int keys_first = s < tokens ? s : tokens;
+        const int keys_second = tokens - keys_first;
+        const int keys = keys_first > keys_second ? keys_first : keys_second;
+        const int cost = chunks * 1024 + keys;
+        if (cost < best_cost) {
+            best_cost = cost;
+            *split = s;
+            *o_col = o;
+        }
+    }
+    return best_cost < (1 << 30);
+}
+
+template <int ElemBytes>
+int launch_typed(const void* qkv, void* context, int batch, int tokens, int heads, float scale,
+                 bool round_output, const host::DeviceContext& device, cudaStream_t stream);
+
 int launch_bf16_pipelined(const void* qkv, void* context, int batch, int tokens, int heads,
                           float scale, const host::DeviceContext& device, cudaStream_t stream) {
     const int n_keys = (tokens + 15) / 16 * 16;
     const int q_tiles = (tokens + kTileQ - 1) / kTileQ;
     const int row = 3 * heads * kHeadDim;
     const int e = heads * kHeadDim;
+    const int buffer_bytes = (q_tiles * kTileQ * 128 + 2 * n_keys * 128 + 1023) / 1024 * 1024;
+    int split = 0;
+    int o_col = 0;
+    if (pipe_smem_bytes(buffer_bytes) > 227 * 1024 || !choose_split(tokens, n_keys, &split, &o_col)) {
+        // Two buffers do not fit next to the slabs (more than 240 tokens): one pair at a time.
+        return launch_typed<2>(qkv, context, batch, tokens, heads, scale, false, device, stream);
+    }
 
     host::TmaTensor tq;
     tq.base = qkv;
@@ -678,9 +780,10 @@ int launch_bf16_pipelined(const void* qkv, void* context, int batch, int tokens,
     tc.dims[2] = static_cast<uint64_t>(batch);
     tc.strides_bytes[0] = static_cast<uint64_t>(e) * 2;
     tc.strides_bytes[1] = static_cast<uint64_t>(e) * tokens * 2;
-    tc.box[0] = 64;
+    tc.box[0] = 32;
     tc.box[1] = 32;
     tc.box[2] = 1;
+    tc.swizzle = CU_TENSOR_MAP_SWIZZLE_64B;
 
     CUtensorMap map_q;
     CUtensorMap map_kv;
@@ -695,12 +798,14 @@ int launch_bf16_pipelined(const void* qkv, void* context, int batch, int tokens,
     params.n_keys = n_keys;
     params.q_tiles = q_tiles;
     params.pairs = batch * heads;
-    params.buffer_bytes = (q_tiles * kTileQ * 128 + 2 * n_keys * 128 + 1023) / 1024 * 1024;
+    params.buffer_bytes = buffer_bytes;
+    params.split = split;
+    params.o_col = o_col;
     params.scale = scale;
     params.scale_log2 = scale * 1.4426950408889634F;
     params.status = device.status;
 
-    const int smem = 1024 + 2 * params.buffer_bytes + 8 * kPipeSlabBytes + 8 * 13 + 16;
+    const int smem = pipe_smem_bytes(buffer_bytes);
     auto* kernel = &attention_bf16_pipelined;
     static std::once_flag once;
     static cudaError_t attribute_error = cudaSuccess;

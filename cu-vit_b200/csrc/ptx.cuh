@@ -106,6 +106,12 @@ __device__ __forceinline__ void grid_launch_dependents() {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
+// Synchronises `threads` threads (a multiple of 32) on hardware barrier `id` (1..15; 0 is
+// __syncthreads), ordering their shared-memory accesses.
+__device__ __forceinline__ void named_barrier_sync(uint32_t id, uint32_t threads) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
 // Makes generic-proxy shared-memory writes visible to the async proxy (TMA, tensor core).
 __device__ __forceinline__ void fence_proxy_async_shared() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -389,6 +395,22 @@ __device__ __forceinline__ float ex2_approx(float x) {
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
     return y;
+}
+
+// 2^x for x <= 0 on the FMA pipe, to relieve the special-function unit: x = n + f with n
+// the nearest integer (x + 1.5 * 2^23 leaves n in the low mantissa bits) and f in
+// [-1/2, 1/2]; 2^f from a degree-3 polynomial fitted here by Remez exchange for minimax
+// relative error on [-1/2, 1/2] (7.5e-5, evaluated in FP32); 2^n is added to the exponent
+// field. Arguments below -125 are raised to -125 so the exponent stays normal.
+__device__ __forceinline__ float exp2_poly(float x) {
+    x = fmaxf(x, -125.0F);
+    const float shifted = __fadd_rn(x, 12582912.0F);
+    const float n = __fadd_rn(shifted, -12582912.0F);
+    const float f = __fadd_rn(x, -n);
+    float p = fmaf(0.0551716685F, f, 0.2426111251F);
+    p = fmaf(p, f, 0.6932609677F);
+    p = fmaf(p, f, 0.9999280572F);
+    return __int_as_float(__float_as_int(p) + (__float_as_int(shifted) << 23));
 }
 
 __device__ __forceinline__ float rcp_approx(float x) {

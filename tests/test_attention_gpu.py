@@ -36,9 +36,10 @@ def expected(qkv, batch, tokens, heads):
 
 
 @pytest.mark.parametrize("dtype", [kernels.DTYPE_BF16, kernels.DTYPE_F32], ids=["bf16", "tf32"])
-@pytest.mark.parametrize("batch,tokens,heads", [(1, 1, 1), (2, 17, 2), (1, 64, 3), (3, 128, 2),
-                                                (2, 129, 1), (2, 197, 3), (1, 197, 12),
-                                                (1, 256, 2), (4, 50, 16)])
+@pytest.mark.parametrize("batch,tokens,heads", [(1, 1, 1), (2, 17, 2), (2, 33, 2), (1, 64, 3),
+                                                (1, 97, 2), (3, 128, 2), (2, 129, 1),
+                                                (2, 197, 3), (1, 197, 12), (2, 225, 2),
+                                                (1, 241, 1), (1, 256, 2), (4, 50, 16)])
 def test_fused_attention_matches_reference_attention(dtype, batch, tokens, heads, cuda):
     rng = np.random.default_rng(tokens * 13 + heads + batch)
     qkv = rng.standard_normal(batch * tokens * 3 * heads * 64).astype(np.float32)

@@ -270,5 +270,44 @@ def test_baseline_configs_full_batch(label, config, batch, precision, seed, tol,
     want = oracle.vit_forward(config, weights, tensor_specs(config), picked)
     err = np.abs(got[sample] - want).max()
     assert err <= tol, f"{label}: max-abs logit error {err:.3g}"
-    assert (got[sample].argmax(1) == want.argmax(1)).all(), f"{label}: top-1 differs"
+    assert_top1_outside_ties(got[sample], want, err, label)
     model.close()
+
+
+def top1_margin(logits):
+    ordered = np.sort(logits, axis=1)
+    return ordered[:, -1] - ordered[:, -2]
+
+
+def assert_top1_outside_ties(got, want, err, label):
+    """Top-1 must agree wherever the reference's top-1 margin exceeds twice the max-abs
+    error: only a near-tie can flip under an error that small, and random-init weights give
+    some (e.g. a 0.005 margin against BF16's ~1e-2 logit error)."""
+    agree = got.argmax(1) == want.argmax(1)
+    margin = top1_margin(want)
+    assert (agree | (margin <= 2 * err)).all(), (
+        f"{label}: top-1 differs with margins {margin[~agree]} above 2 x {err:.3g}")
+
+
+def test_bf16_top1_agreement_vit_b_full_batch(cuda):
+    """Top-1 on all 256 images of ViT-B/16: BF16 logits against the FP32 path (pinned to the
+    oracle at 1e-4), max-abs <= 3e-2. With random-init weights 14 of these images have a
+    top-1 margin below 0.01, under the BF16 logit error, and 3 of them flip (98.8%
+    agreement, margins 0.0005-0.005); so the check is: no flip outside a near-tie (margin <=
+    2 x max-abs error) and agreement >= 98%."""
+    config = VitConfig(embed_dim=768, heads=12, mlp_hidden=3072)
+    batch = 256
+    weights = random_weights(config, 3)
+    images = np.random.default_rng(3).standard_normal(
+        batch * config.image_elements()).astype(np.float32)
+    bf16 = VisionTransformer(config, weights, max_batch=batch, precision=PRECISION_BF16)
+    got = model_logits(bf16, images, batch, cuda)
+    bf16.close()
+    fp32 = VisionTransformer(config, weights, max_batch=batch, precision=PRECISION_FP32)
+    want = model_logits(fp32, images, batch, cuda)
+    fp32.close()
+    err = np.abs(got - want).max()
+    assert err <= BF16_TOL, f"max-abs logit error {err:.3g}"
+    assert_top1_outside_ties(got, want, err, "vit-b b256 bf16 vs fp32")
+    agree = (got.argmax(1) == want.argmax(1)).mean()
+    assert agree >= 0.98, f"top-1 agreement {agree:.4f}"
