@@ -320,6 +320,14 @@ int prepare(const Resolved& r, Plan* plan) {
     const int block_k = kSwizzleBytes / e;
     const int atom = kSwizzleBytes / e;
     const int bn = choose_block_n(p.n, split);
+    // CTA pairs for BF16 with the weights' K-major layout and 256-wide tiles, once there are
+    // at least as many 256-row tiles as SMs (two per pair), so the pairs stay busy. A GELU
+    // epilogue keeps the one-CTA kernel: its issue slots, not operand traffic, bound it
+    // (ViT-B/16 FC1 on B200: 220 us one-CTA, 224 us paired; QKV 153 vs 145 us).
+    const long long pair_tiles =
+        ((p.m + 2LL * kBlockM - 1) / (2 * kBlockM)) * ((p.n + bn - 1) / bn) * p.batch.count;
+    const bool pair = bf16 && r.transposed && bn == 256 && !p.epilogue.gelu &&
+                      pairs_enabled() && pair_tiles >= context->sm_count;
     const CUtensorMapDataType type =
         bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
 
@@ -348,7 +356,7 @@ int prepare(const Resolved& r, Plan* plan) {
         tb.dims[0] = static_cast<uint64_t>(p.k);
         tb.dims[1] = static_cast<uint64_t>(p.n);
         tb.box[0] = static_cast<uint32_t>(block_k);
-        tb.box[1] = static_cast<uint32_t>(bn);
+        tb.box[1] = static_cast<uint32_t>(pair ? bn / 2 : bn);
     } else {
         tb.dims[0] = static_cast<uint64_t>(p.n);
         tb.dims[1] = static_cast<uint64_t>(p.k);
@@ -373,7 +381,8 @@ int prepare(const Resolved& r, Plan* plan) {
         return CUVIT_OK; // the driver refused this shape; the SIMT path still serves it
     }
 
-    const long long m_tiles = (p.m + kBlockM - 1) / kBlockM;
+    const int block_m = pair ? 2 * kBlockM : kBlockM;
+    const long long m_tiles = (p.m + block_m - 1) / block_m;
     const long long n_tiles = (p.n + bn - 1) / bn;
     const long long total = m_tiles * n_tiles * p.batch.count;
     if (total > 0x7FFFFFFFLL) {
@@ -451,6 +460,7 @@ int prepare(const Resolved& r, Plan* plan) {
     plan->block_n = bn;
     plan->b_mn_major = !r.transposed;
     plan->split = split;
+    plan->pair = pair;
     plan->grid = static_cast<int>(total < context->sm_count ? total : context->sm_count);
     plan->path = Path::kTensorCore;
     return CUVIT_OK;
@@ -461,6 +471,9 @@ int launch(const Plan& plan, cudaStream_t stream) {
     case Path::kTensorCore:
         if (plan.split) {
             return launch_tc_split(plan, stream);
+        }
+        if (plan.pair) {
+            return launch_tc_pair(plan, stream);
         }
         return plan.elem_bytes == 2 ? launch_tc_bf16(plan, stream) : launch_tc_tf32(plan, stream);
     case Path::kSimt:

@@ -38,6 +38,7 @@ struct Plan {
     int block_n = 128;
     bool b_mn_major = false;
     bool split = false;
+    bool pair = false; // CTA-pair kernel (256-row tiles, B map boxes of block_n / 2 rows)
     int grid = 0;
     // SIMT path
     Resolved resolved{};
@@ -58,6 +59,11 @@ int launch(const Plan& plan, cudaStream_t stream);
 int launch_tc_bf16(const Plan& plan, cudaStream_t stream);
 int launch_tc_tf32(const Plan& plan, cudaStream_t stream);
 int launch_tc_split(const Plan& plan, cudaStream_t stream);
+int launch_tc_pair(const Plan& plan, cudaStream_t stream);
+
+// Whether large BF16 GEMMs may use the CTA-pair kernel: on unless the environment sets
+// CUVIT_GEMM_PAIRS=0 (which keeps every GEMM on the one-CTA kernel).
+bool pairs_enabled();
 
 // Dynamic shared memory the chosen instantiation needs.
 int tc_smem_bytes(int elem_bytes, int block_n, bool split);

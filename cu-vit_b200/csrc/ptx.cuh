@@ -91,6 +91,60 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, unsigne
     }
 }
 
+// Waits up to limit_ns for a phase regardless of the status word: used after a failure to
+// let this thread's own copies in flight land before the CTA exits.
+__device__ __forceinline__ bool mbar_drain_wait(uint32_t bar, uint32_t parity,
+                                                unsigned long long limit_ns = 100000000ull) {
+    const unsigned long long start = global_timer_ns();
+    while (!mbar_try_wait(bar, parity)) {
+        if (global_timer_ns() - start > limit_ns) {
+            return false;
+        }
+    }
+    return true;
+}
+
+// ---- thread-block clusters --------------------------------------------------------------
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+    uint32_t rank;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(rank));
+    return rank;
+}
+
+__device__ __forceinline__ uint32_t cluster_id_x() {
+    uint32_t id;
+    asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(id));
+    return id;
+}
+
+__device__ __forceinline__ uint32_t cluster_count_x() {
+    uint32_t count;
+    asm volatile("mov.u32 %0, %%nclusterid.x;" : "=r"(count));
+    return count;
+}
+
+// The shared::cluster address of shared-memory offset `addr` in CTA `rank` of this cluster.
+__device__ __forceinline__ uint32_t map_to_rank(uint32_t addr, uint32_t rank) {
+    uint32_t mapped;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(mapped) : "r"(addr), "r"(rank));
+    return mapped;
+}
+
+// Every thread of every CTA in the cluster; orders shared-memory accesses across the cluster.
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\t"
+                 "barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// One arrival on an mbarrier anywhere in the cluster (a shared::cluster address). As for
+// local barriers, the waiting side uses mbar_wait(): data handed over this way lives in
+// shared memory or TMEM, and every consumer reaches it through the async proxy or tcgen05
+// after that wait.
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+
 // Programmatic dependent launch: kernels are launched so that they may start while the
 // previous kernel in the stream is still finishing. Each kernel runs its prologue (barrier
 // set-up, TMEM allocation, descriptor prefetch), then waits here until the previous grid has
@@ -243,6 +297,50 @@ __device__ __forceinline__ void tc_fence_after() {
 }
 
 // Arrives on the mbarrier once all tcgen05 operations this thread issued so far complete.
+// ---- CTA pairs (cta_group::2): one MMA spans the tensor memory of both CTAs -------------
+
+// Both CTAs of the pair call these from the same warp index, with the same slot offset.
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t dst_smem, uint32_t columns) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     dst_smem),
+                 "r"(columns)
+                 : "memory");
+}
+
+__device__ __forceinline__ void tmem_relinquish_pair() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t columns) {
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr),
+                 "r"(columns)
+                 : "memory");
+}
+
+// D (M = 256: rows 0..127 in this CTA's TMEM, 128..255 in the peer's) (+)= A * B, where each
+// CTA holds its own 128 rows of A and half of B's N rows at the same shared-memory offsets.
+// Issued by the pair's even CTA only.
+__device__ __forceinline__ void mma_pair_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                             uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t"
+        ".reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t"
+        "}\n" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// One arrival on the mbarrier at shared::cluster address `bar` (in either CTA of the pair)
+// once every pair MMA this thread has issued so far has completed.
+__device__ __forceinline__ void tc_commit_pair(uint32_t cluster_bar) {
+    asm volatile(
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+            cluster_bar)
+        : "memory");
+}
+
 __device__ __forceinline__ void tc_commit(uint32_t bar) {
     asm volatile(
         "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)

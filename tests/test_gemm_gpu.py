@@ -360,3 +360,63 @@ def test_device_timeout_is_reported_and_the_context_survives(cuda):
         kernels.device_status()
     assert kernels.device_status() == 0
     check_case(64, 64, 64, T, True, 1.0, kernels.MATH_BF16, cuda)
+
+
+# Large BF16 GEMMs with the weights' [N, K] layout and no GELU run on the CTA-pair kernel
+# (256-row tiles over two SMs) once there are at least as many 256-row tiles as SMs; these
+# shapes all get there. Reference: the same bfloat16 operands multiplied in FP32 by PyTorch
+# (TF32 off).
+PAIR_CASES = [
+    # m, n, k, count, c_dtype, gelu, accumulate, with_bias
+    (4261, 2304, 768, 1, kernels.DTYPE_F32, False, False, True),     # ragged last tile
+    (4261, 2304, 768, 1, kernels.DTYPE_BF16, False, False, True),    # bf16 output
+    (50432, 768, 768, 1, kernels.DTYPE_F32, False, True, True),      # residual reduce-add
+    (2048, 2560, 64, 2, kernels.DTYPE_F32, False, False, False),     # one k-block, batched
+    (4096, 2560, 8000, 1, kernels.DTYPE_F32, False, False, True),    # long K, ragged k-block
+]
+
+
+@pytest.mark.parametrize("m,n,k,count,c_dtype,gelu,accumulate,with_bias", PAIR_CASES,
+                         ids=[f"{c[0]}x{c[1]}x{c[2]}x{c[3]}" + ("-gelu" if c[5] else "") +
+                              ("-acc" if c[6] else "") for c in PAIR_CASES])
+def test_cta_pair_gemm_against_torch_fp32(m, n, k, count, c_dtype, gelu, accumulate, with_bias,
+                                          cuda):
+    torch = cuda
+    assert not torch.backends.cuda.matmul.allow_tf32
+    g = torch.Generator(device="cuda").manual_seed(m + n + k)
+    a = torch.randn(count, m, k, device="cuda", generator=g).to(torch.bfloat16)
+    b = torch.randn(count, n, k, device="cuda", generator=g).to(torch.bfloat16)
+    bias = torch.randn(n, device="cuda", generator=g) if with_bias else None
+    c0 = torch.randn(count, m, n, device="cuda", generator=g)
+    out_dtype = torch.bfloat16 if c_dtype == kernels.DTYPE_BF16 else torch.float32
+    c = c0.to(out_dtype, copy=True) if accumulate else torch.full(
+        (count, m, n), float("nan"), device="cuda", dtype=out_dtype)
+    problem = gemm_problem(m, n, k, T)
+    problem.batch.count = count
+    problem.batch.stride_a = m * k
+    problem.batch.stride_b = n * k
+    problem.batch.stride_c = m * n
+    problem.epilogue.gelu = gelu
+    problem.epilogue.accumulate = accumulate
+    kernels.launch_gemm_ex(a, b, bias, c, problem, c_dtype=c_dtype, math=kernels.MATH_BF16)
+    torch.cuda.synchronize()
+    assert kernels.device_status() == 0
+
+    af, bf = a.float(), b.float()
+    want = torch.bmm(af, bf.transpose(1, 2))
+    scale = torch.bmm(af.abs(), bf.abs().transpose(1, 2))
+    if bias is not None:
+        want = want + bias
+    if gelu:
+        want = torch.nn.functional.gelu(want)
+    if accumulate:
+        want = want + c0.to(out_dtype).float()
+    got = c.float()
+    assert torch.isfinite(got).all(), "rows or columns were left unwritten"
+    if c_dtype == kernels.DTYPE_BF16:
+        # one bf16 rounding of the result (2^-8 relative) on top of the accumulation
+        tol = want.abs() * 2.0 ** -8 + scale * 1e-5 + 1e-6
+    else:
+        tol = scale * 1e-5 + 1e-6
+    excess = ((got - want).abs() - tol).max().item()
+    assert excess <= 0, f"error exceeds the bound by {excess:.3g}"
