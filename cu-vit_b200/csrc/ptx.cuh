@@ -520,19 +520,20 @@ __device__ __forceinline__ float rcp_approx(float x) {
 // GELU with erf evaluated by Abramowitz & Stegun, Handbook of Mathematical Functions,
 // formula 7.1.26 (|error| <= 1.5e-7 on erf), using the hardware reciprocal and exponential.
 // For BF16 outputs, whose rounding (2^-9 relative) is far coarser than the approximation;
-// FP32 and TF32 outputs keep gelu_erf.
+// FP32 and TF32 outputs keep gelu_erf. Since x * erf(x / sqrt 2) = |x| * erf(|x| / sqrt 2),
+//   GELU(x) = max(x, 0) - |x|/2 * erfc(|x| / sqrt 2),  erfc(z) ~= t * P(t) * exp(-z^2),
+// which needs no sign handling and never forms 1 - erf (whose cancellation cost up to 15%
+// relative error where |GELU| ~ 1e-6): relative error <= 1.7e-3 wherever |GELU| >= 1e-6.
 __device__ __forceinline__ float gelu_bf16_output(float x) {
-    const float z = fabsf(x) * 0.7071067811865475F;
-    const float t = rcp_approx(fmaf(0.3275911F, z, 1.0F));
+    const float magnitude = fabsf(x);
+    const float t = rcp_approx(fmaf(0.3275911F * 0.7071067811865475F, magnitude, 1.0F));
     float poly = fmaf(t, 1.061405429F, -1.453152027F);
     poly = fmaf(t, poly, 1.421413741F);
     poly = fmaf(t, poly, -0.284496736F);
     poly = fmaf(t, poly, 0.254829592F);
-    poly *= t;
-    const float tail = ex2_approx(-(z * z) * 1.4426950408889634F);
-    const float erf_abs = fmaf(-poly, tail, 1.0F);
-    const float half_x = 0.5F * x;
-    return fmaf(half_x, copysignf(erf_abs, x), half_x);
+    poly *= 0.5F * magnitude * t;
+    const float tail = ex2_approx(x * (x * (-0.5F * 1.4426950408889634F)));
+    return fmaf(-poly, tail, fmaxf(x, 0.0F));
 }
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float low, float high) {

