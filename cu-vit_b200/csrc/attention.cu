@@ -41,6 +41,7 @@ struct Params {
     float scale;
     void* context;
     int round_output; // FP32 path: store the context rounded to TF32 values
+    int reverse;      // walk (image, head) pairs from the last to the first
     unsigned* status;
 };
 
@@ -90,8 +91,10 @@ __global__ void __launch_bounds__(kThreads)
 
     const int warp = threadIdx.x / 32;
     const int lane = threadIdx.x % 32;
-    const int image = blockIdx.x / p.heads;
-    const int head = blockIdx.x - image * p.heads;
+    const int job = p.reverse ? static_cast<int>(gridDim.x - 1 - blockIdx.x)
+                              : static_cast<int>(blockIdx.x);
+    const int image = job / p.heads;
+    const int head = job - image * p.heads;
 
     if (threadIdx.x == 0) {
         dev::mbar_init(bar_load, 1);
@@ -345,6 +348,7 @@ struct PipeParams {
     int buffer_bytes; // one Q/K/V buffer, 1024-aligned
     int split;        // first key column of the second softmax warpgroup
     int o_col;        // first TMEM column of O within a tile's region
+    int reverse;      // walk (image, head) pairs from the last to the first
     float scale;
     float scale_log2;
     unsigned* status;
@@ -428,8 +432,9 @@ __global__ void __launch_bounds__(kPipeThreads, 1)
             if (!dev::mbar_wait(bar(kBufEmpty, b), (use & 1u) ^ 1u, p.status)) {
                 break;
             }
-            const int image = pair / p.heads;
-            const int head = pair - image * p.heads;
+            const int job = p.reverse ? p.pairs - 1 - pair : pair;
+            const int image = job / p.heads;
+            const int head = job - image * p.heads;
             dev::mbar_arrive_expect_tx(bar(kBufFull, b), bytes);
             for (int t = 0; t < p.q_tiles; ++t) {
                 const int c[3] = {head * kHeadDim, t * kTileQ, image};
@@ -682,8 +687,9 @@ __global__ void __launch_bounds__(kPipeThreads, 1)
                 dev::fence_proxy_async_shared();
                 __syncwarp();
                 if (lane == 0) {
-                    const int image = pair / p.heads;
-                    const int head = pair - image * p.heads;
+                    const int job = p.reverse ? p.pairs - 1 - pair : pair;
+                    const int image = job / p.heads;
+                    const int head = job - image * p.heads;
                     const int coords[3] = {head * kHeadDim + 32 * h,
                                            t * kTileQ + quarter * 32, image};
                     dev::tma_store<false>(&map_ctx, slab_addr, 3, coords);
@@ -801,6 +807,7 @@ int launch_bf16_pipelined(const void* qkv, void* context, int batch, int tokens,
     params.buffer_bytes = buffer_bytes;
     params.split = split;
     params.o_col = o_col;
+    params.reverse = host::reverse_sweep() ? 1 : 0;
     params.scale = scale;
     params.scale_log2 = scale * 1.4426950408889634F;
     params.status = device.status;
@@ -863,6 +870,7 @@ int launch_typed(const void* qkv, void* context, int batch, int tokens, int head
     params.scale_log2 = scale * 1.4426950408889634F;
     params.context = context;
     params.round_output = round_output ? 1 : 0;
+    params.reverse = host::reverse_sweep() ? 1 : 0;
     params.status = device.status;
 
     int smem = 1024 + q_tiles * L::kQTileBytes + 2 * L::kDAtoms * n_keys * 128 + 64;

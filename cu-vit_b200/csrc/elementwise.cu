@@ -87,14 +87,15 @@ __global__ void __launch_bounds__(kThreads)
     layer_norm_warp_kernel(const float* __restrict__ input, long long in_stride,
                            const float* __restrict__ gamma, const float* __restrict__ beta,
                            Out* __restrict__ output, long long out_stride, int rows, int columns,
-                           float epsilon) {
+                           float epsilon, int reverse) {
     dev::grid_dependency_wait();
     dev::grid_launch_dependents();
-    const int row = blockIdx.x * kRowsPerBlock + threadIdx.x / kWarp;
+    const int slot = blockIdx.x * kRowsPerBlock + threadIdx.x / kWarp;
     const int lane = threadIdx.x % kWarp;
-    if (row >= rows) {
+    if (slot >= rows) {
         return;
     }
+    const int row = reverse ? rows - 1 - slot : slot;
     const float4* const in4 = reinterpret_cast<const float4*>(input + row * in_stride);
     const int vectors = columns / 4;
     float4 x[kMaxVec];
@@ -161,11 +162,11 @@ __global__ void __launch_bounds__(kThreads)
     layer_norm_block_kernel(const float* __restrict__ input, long long in_stride,
                             const float* __restrict__ gamma, const float* __restrict__ beta,
                             Out* __restrict__ output, long long out_stride, int columns,
-                            float epsilon) {
+                            float epsilon, int reverse) {
     dev::grid_dependency_wait();
     dev::grid_launch_dependents();
     __shared__ float scratch[kThreads / kWarp];
-    const long long row = blockIdx.x;
+    const long long row = reverse ? gridDim.x - 1 - blockIdx.x : blockIdx.x;
     const float* const x = input + row * in_stride;
     const float origin = x[0];
     float sum = 0.0F;
@@ -466,6 +467,7 @@ int layer_norm_impl(const float* input, long long in_stride, const float* gamma,
         return host::fail(CUVIT_INVALID_ARGUMENT, "layer norm row stride is below the row");
     }
     const int out_bytes = out_dtype == CUVIT_DTYPE_BF16 ? 2 : 4;
+    const int reverse = host::reverse_sweep() ? 1 : 0;
     const bool fast = columns % 4 == 0 && columns <= 4 * kWarp * kMaxVec && aligned(input, 16) &&
                       aligned(gamma, 16) && aligned(beta, 16) && in_stride % 4 == 0 &&
                       aligned(output, 4 * out_bytes) && out_stride % 4 == 0;
@@ -475,10 +477,12 @@ int layer_norm_impl(const float* input, long long in_stride, const float* gamma,
             const unsigned blocks =
                 static_cast<unsigned>((rows + kRowsPerBlock - 1) / kRowsPerBlock);
             host::pdl_launch(layer_norm_warp_kernel<Out>, blocks, kThreads, 0, stream, input,
-                             in_stride, gamma, beta, out, out_stride, rows, columns, epsilon);
+                             in_stride, gamma, beta, out, out_stride, rows, columns, epsilon,
+                             reverse);
         } else {
             host::pdl_launch(layer_norm_block_kernel<Out>, rows, kThreads, 0, stream, input,
-                             in_stride, gamma, beta, out, out_stride, columns, epsilon);
+                             in_stride, gamma, beta, out, out_stride, columns, epsilon,
+                             reverse);
         }
     };
     if (out_dtype == CUVIT_DTYPE_BF16) {

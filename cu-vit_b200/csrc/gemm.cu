@@ -420,6 +420,7 @@ int prepare(const Resolved& r, Plan* plan) {
                         : 0;
     q.accumulate = p.epilogue.accumulate ? 1 : 0;
     q.gelu = p.epilogue.gelu ? 1 : 0;
+    q.reverse = host::reverse_sweep() ? 1 : 0;
     q.status = context->status;
     q.bias_vector_ok =
         r.bias != nullptr && reinterpret_cast<uintptr_t>(r.bias) % 16 == 0 ? 1 : 0;

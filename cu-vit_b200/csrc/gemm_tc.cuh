@@ -56,8 +56,14 @@ struct TcParams {
     int c_tma;       // write C with TMA stores (reduce-adds when accumulating)
     int c_vector_ok; // direct path: 16-byte vector stores of whole chunks are aligned
     int accumulate, gelu;
+    int reverse; // walk the output tiles from the last to the first
     unsigned* status;
 };
+
+// The output tile a CTA's t-th tile index stands for, in the launch's sweep order.
+__device__ __forceinline__ int ordered_tile(const TcParams& p, int t) {
+    return p.reverse ? p.total_tiles - 1 - t : t;
+}
 
 template <int ElemBytes, int BN, bool Split>
 struct TcShape {
@@ -379,8 +385,9 @@ __global__ void __launch_bounds__(TcShape<ElemBytes, BN, Split>::kThreads, 1)
         uint32_t phase = 0;
         bool ok = true;
         for (int tile = blockIdx.x; tile < p.total_tiles && ok; tile += gridDim.x) {
-            const int entry = tile / per_entry;
-            const int rest = tile - entry * per_entry;
+            const int ordered = ordered_tile(p, tile);
+            const int entry = ordered / per_entry;
+            const int rest = ordered - entry * per_entry;
             const int m_block = rest / p.n_tiles;
             const int n_block = rest - m_block * p.n_tiles;
             int index, outer;
@@ -515,8 +522,9 @@ __global__ void __launch_bounds__(TcShape<ElemBytes, BN, Split>::kThreads, 1)
         }
         int local = 0;
         for (int tile = blockIdx.x; tile < p.total_tiles; tile += gridDim.x, ++local) {
-            const int entry = tile / per_entry;
-            const int rest = tile - entry * per_entry;
+            const int ordered = ordered_tile(p, tile);
+            const int entry = ordered / per_entry;
+            const int rest = ordered - entry * per_entry;
             const int m_block = rest / p.n_tiles;
             const int n_block = rest - m_block * p.n_tiles;
             int index, outer;

@@ -127,8 +127,9 @@ __global__ void __launch_bounds__(PairShape<BN>::kThreads, 1)
         uint32_t phase = 0;
         bool ok = true;
         for (int tile = pair_id; tile < p.total_tiles && ok; tile += pair_count) {
-            const int entry = tile / per_entry;
-            const int rest = tile - entry * per_entry;
+            const int ordered = ordered_tile(p, tile);
+            const int entry = ordered / per_entry;
+            const int rest = ordered - entry * per_entry;
             const int m_block = rest / p.n_tiles;
             const int n_block = rest - m_block * p.n_tiles;
             int index, outer;
@@ -242,8 +243,9 @@ __global__ void __launch_bounds__(PairShape<BN>::kThreads, 1)
         }
         int local = 0;
         for (int tile = pair_id; tile < p.total_tiles; tile += pair_count, ++local) {
-            const int entry = tile / per_entry;
-            const int rest = tile - entry * per_entry;
+            const int ordered = ordered_tile(p, tile);
+            const int entry = ordered / per_entry;
+            const int rest = ordered - entry * per_entry;
             const int m_block = rest / p.n_tiles;
             const int n_block = rest - m_block * p.n_tiles;
             int index, outer;

@@ -95,6 +95,18 @@ int current_context(const DeviceContext** context) {
 
 bool is_blackwell(const DeviceContext& context) { return context.major == 10; }
 
+namespace {
+thread_local bool t_reverse_sweep = false;
+} // namespace
+
+bool reverse_sweep() { return t_reverse_sweep; }
+
+ReverseSweep::ReverseSweep(bool reverse) : previous_(t_reverse_sweep) {
+    t_reverse_sweep = reverse;
+}
+
+ReverseSweep::~ReverseSweep() { t_reverse_sweep = previous_; }
+
 bool pdl_enabled() {
     static const bool enabled = []() {
         const char* value = std::getenv("CUVIT_PDL");

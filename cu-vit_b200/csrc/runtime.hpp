@@ -65,6 +65,23 @@ void pdl_launch(void (*kernel)(KernelArgs...), dim3 grid, dim3 block, size_t sme
     cudaLaunchKernelEx(&config, kernel, std::forward<Args>(args)...);
 }
 
+// Order in which launches made on this thread walk their output tiles, rows or (image, head)
+// pairs: first to last (the default), or last to first while a ReverseSweep is alive. Results
+// do not depend on it. The model runner alternates it from one launch to the next, so each
+// kernel starts on the rows the previous one wrote last, which are still in L2.
+bool reverse_sweep();
+
+class ReverseSweep {
+  public:
+    explicit ReverseSweep(bool reverse);
+    ~ReverseSweep();
+    ReverseSweep(const ReverseSweep&) = delete;
+    ReverseSweep& operator=(const ReverseSweep&) = delete;
+
+  private:
+    bool previous_;
+};
+
 struct DeviceContext {
     int device = -1;
     int sm_count = 0;
