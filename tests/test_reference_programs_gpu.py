@@ -1,9 +1,10 @@
 """The reference's own test programs, unchanged, against this library.
 
 oracle/_ref/gemm_test_b200 and elementwise_test_b200 are the reference's tests/gemm_test.cu and
-tests/elementwise_test.cu compiled against include/cuvit/kernels.hpp and linked with
-libcuvit_b200.so (oracle/Makefile, target ref-tests). Each exits 0 and prints PASS only if every
-check in it holds at the reference's own tolerances.
+tests/elementwise_test.cu compiled against include/cuvit/kernels.hpp; vit_test_b200 is its
+tests/vit_test.cu compiled against include/cuvit/vit.hpp (with the reference's own WeightFile
+and CPU reference); all linked with libcuvit_b200.so (oracle/Makefile, target ref-tests). Each
+exits 0 and prints PASS only if every check in it holds at the reference's own tolerances.
 """
 
 from __future__ import annotations
@@ -14,7 +15,7 @@ import subprocess
 import pytest
 
 ROOT = pathlib.Path(__file__).resolve().parents[1]
-PROGRAMS = ["gemm_test_b200", "elementwise_test_b200"]
+PROGRAMS = ["gemm_test_b200", "elementwise_test_b200", "vit_test_b200"]
 
 pytestmark = pytest.mark.gpu
 
