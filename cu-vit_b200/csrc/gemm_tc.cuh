@@ -143,10 +143,14 @@ __device__ __forceinline__ void apply_epilogue(float (&v)[Cols], const TcParams&
 #pragma unroll
             for (int q = 0; q < Cols / 4; ++q) {
                 const float4 b = __ldg(b4 + q);
-                v[4 * q] += b.x;
-                v[4 * q + 1] += b.y;
-                v[4 * q + 2] += b.z;
-                v[4 * q + 3] += b.w;
+                const float2 lo = dev::f32x2_split(
+                    dev::add_f32x2(dev::f32x2(v[4 * q], v[4 * q + 1]), dev::f32x2(b.x, b.y)));
+                const float2 hi = dev::f32x2_split(dev::add_f32x2(
+                    dev::f32x2(v[4 * q + 2], v[4 * q + 3]), dev::f32x2(b.z, b.w)));
+                v[4 * q] = lo.x;
+                v[4 * q + 1] = lo.y;
+                v[4 * q + 2] = hi.x;
+                v[4 * q + 3] = hi.y;
             }
         } else {
 #pragma unroll
@@ -160,8 +164,10 @@ __device__ __forceinline__ void apply_epilogue(float (&v)[Cols], const TcParams&
     if (p.gelu) {
         if (p.c_kind == 1) {
 #pragma unroll
-            for (int j = 0; j < Cols; ++j) {
-                v[j] = dev::gelu_bf16_output(v[j]);
+            for (int j = 0; j < Cols; j += 2) {
+                const float2 g = dev::gelu_bf16_output2(v[j], v[j + 1]);
+                v[j] = g.x;
+                v[j + 1] = g.y;
             }
         } else {
 #pragma unroll

@@ -495,6 +495,58 @@ __device__ __forceinline__ float ex2_approx(float x) {
     return y;
 }
 
+// Two FP32 values in one 64-bit register for sm_100's packed FP32 arithmetic: add, mul and
+// fma .rn.f32x2 perform two IEEE round-to-nearest operations per instruction, so code written
+// with them gives the results of the scalar operations in half the issue slots.
+__device__ __forceinline__ uint64_t f32x2(float low, float high) {
+    uint64_t packed;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(packed) : "f"(low), "f"(high));
+    return packed;
+}
+
+__device__ __forceinline__ float2 f32x2_split(uint64_t packed) {
+    float2 pair;
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(pair.x), "=f"(pair.y) : "l"(packed));
+    return pair;
+}
+
+__device__ __forceinline__ uint64_t fma_f32x2(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+
+__device__ __forceinline__ uint64_t mul_f32x2(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+
+__device__ __forceinline__ uint64_t add_f32x2(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+
+__device__ __forceinline__ uint64_t sub_f32x2(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+
+// Three-operand maximum / minimum (sm_100): two new values per instruction in a reduction.
+__device__ __forceinline__ float max3(float a, float b, float c) {
+    float d;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
+
+__device__ __forceinline__ float min3(float a, float b, float c) {
+    float d;
+    asm("min.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
+
 // 2^x for x <= 0 on the FMA pipe, to relieve the special-function unit: x = n + f with n
 // the nearest integer (x + 1.5 * 2^23 leaves n in the low mantissa bits) and f in
 // [-1/2, 1/2]; 2^f from a degree-3 polynomial fitted here by Remez exchange for minimax
@@ -509,6 +561,23 @@ __device__ __forceinline__ float exp2_poly(float x) {
     p = fmaf(p, f, 0.6932609677F);
     p = fmaf(p, f, 0.9999280572F);
     return __int_as_float(__float_as_int(p) + (__float_as_int(shifted) << 23));
+}
+
+// exp2_poly on two values, the additions and the polynomial two per instruction: the same
+// operations in the same order, so the same results.
+__device__ __forceinline__ float2 exp2_poly2(float x0, float x1) {
+    const uint64_t x = f32x2(fmaxf(x0, -125.0F), fmaxf(x1, -125.0F));
+    const uint64_t shifted = add_f32x2(x, f32x2(12582912.0F, 12582912.0F));
+    const uint64_t n = add_f32x2(shifted, f32x2(-12582912.0F, -12582912.0F));
+    const uint64_t f = sub_f32x2(x, n);
+    uint64_t p = fma_f32x2(f32x2(0.0551716685F, 0.0551716685F), f,
+                           f32x2(0.2426111251F, 0.2426111251F));
+    p = fma_f32x2(p, f, f32x2(0.6932609677F, 0.6932609677F));
+    p = fma_f32x2(p, f, f32x2(0.9999280572F, 0.9999280572F));
+    const float2 poly = f32x2_split(p);
+    const float2 scale = f32x2_split(shifted);
+    return make_float2(__int_as_float(__float_as_int(poly.x) + (__float_as_int(scale.x) << 23)),
+                       __int_as_float(__float_as_int(poly.y) + (__float_as_int(scale.y) << 23)));
 }
 
 __device__ __forceinline__ float rcp_approx(float x) {
@@ -534,6 +603,30 @@ __device__ __forceinline__ float gelu_bf16_output(float x) {
     poly *= 0.5F * magnitude * t;
     const float tail = ex2_approx(x * (x * (-0.5F * 1.4426950408889634F)));
     return fmaf(-poly, tail, fmaxf(x, 0.0F));
+}
+
+// gelu_bf16_output on two values: the same operations in the same order, with the
+// polynomial's coefficients scaled by -1/2 (exact) so its sign and halving need no separate
+// steps -- the same results as two scalar calls, the multiply-adds two per instruction.
+__device__ __forceinline__ float2 gelu_bf16_output2(float x0, float x1) {
+    const float m0 = fabsf(x0);
+    const float m1 = fabsf(x1);
+    const uint64_t m = f32x2(m0, m1);
+    const float2 den = f32x2_split(fma_f32x2(
+        f32x2(0.3275911F * 0.7071067811865475F, 0.3275911F * 0.7071067811865475F), m,
+        f32x2(1.0F, 1.0F)));
+    const uint64_t t = f32x2(rcp_approx(den.x), rcp_approx(den.y));
+    uint64_t poly = fma_f32x2(t, f32x2(-0.5F * 1.061405429F, -0.5F * 1.061405429F),
+                              f32x2(0.5F * 1.453152027F, 0.5F * 1.453152027F));
+    poly = fma_f32x2(t, poly, f32x2(-0.5F * 1.421413741F, -0.5F * 1.421413741F));
+    poly = fma_f32x2(t, poly, f32x2(0.5F * 0.284496736F, 0.5F * 0.284496736F));
+    poly = fma_f32x2(t, poly, f32x2(-0.5F * 0.254829592F, -0.5F * 0.254829592F));
+    poly = mul_f32x2(poly, mul_f32x2(m, t));
+    const uint64_t x = f32x2(x0, x1);
+    constexpr float kHalfLog2e = -0.5F * 1.4426950408889634F;
+    const float2 arg = f32x2_split(mul_f32x2(x, mul_f32x2(x, f32x2(kHalfLog2e, kHalfLog2e))));
+    const uint64_t tail = f32x2(ex2_approx(arg.x), ex2_approx(arg.y));
+    return f32x2_split(fma_f32x2(poly, tail, f32x2(fmaxf(x0, 0.0F), fmaxf(x1, 0.0F))));
 }
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float low, float high) {
