@@ -274,6 +274,27 @@ def test_baseline_configs_full_batch(label, config, batch, precision, seed, tol,
     model.close()
 
 
+def test_vit_l_bf16_against_fp32_path(cuda):
+    """BASELINE config 5's model (ViT-L/16: E = 1024, 16 heads, depth 24, MLP 4096) at 16
+    images per GPU: BF16 logits within 3e-2 of the FP32-faithful path (which the oracle pins
+    at 1e-4 on the smaller configs), top-1 identical outside near-ties."""
+    config = VitConfig(embed_dim=1024, depth=24, heads=16, mlp_hidden=4096)
+    batch = 16
+    weights = random_weights(config, 4)
+    images = np.random.default_rng(4).standard_normal(
+        batch * config.image_elements()).astype(np.float32)
+    bf16 = VisionTransformer(config, weights, max_batch=batch, precision=PRECISION_BF16)
+    got = model_logits(bf16, images, batch, cuda)
+    bf16.close()
+    fp32 = VisionTransformer(config, weights, max_batch=batch, precision=PRECISION_FP32)
+    want = model_logits(fp32, images, batch, cuda)
+    fp32.close()
+    assert np.isfinite(got).all()
+    err = np.abs(got - want).max()
+    assert err <= BF16_TOL, f"ViT-L max-abs logit error {err:.3g}"
+    assert_top1_outside_ties(got, want, err, "vit-l b16 bf16 vs fp32")
+
+
 def top1_margin(logits):
     ordered = np.sort(logits, axis=1)
     return ordered[:, -1] - ordered[:, -2]
