@@ -432,6 +432,45 @@ __global__ void extract_patches_kernel(const float* __restrict__ images, Out* __
     }
 }
 
+// The same gather, one block per (image, row of patches): the block reads that strip of the
+// image (channels x patch rows x width) with coalesced 16-byte loads along image rows and
+// writes each 4-value group to its patch, so consecutive threads write consecutive 4-value
+// groups of a patch row. Needs patch and width multiples of 4.
+template <typename Out>
+__global__ void __launch_bounds__(kThreads)
+    extract_patch_rows_kernel(const float* __restrict__ images, Out* __restrict__ patches,
+                              int channels, int height, int width, int patch, int across,
+                              int patch_rows, int reverse) {
+    dev::grid_dependency_wait();
+    dev::grid_launch_dependents();
+    const int slot = static_cast<int>(blockIdx.x);
+    const int strip = reverse ? static_cast<int>(gridDim.x) - 1 - slot : slot;
+    const int image = strip / patch_rows;
+    const int pr = strip - image * patch_rows;
+    const int quads = width / 4;                // float4 per image row
+    const int per_channel = patch * quads;      // float4 per channel of the strip
+    const int count = channels * per_channel;   // float4 in the strip
+    const int area = patch * patch;
+    const long long row_length = static_cast<long long>(channels) * area;
+    const float* const base =
+        images + static_cast<long long>(image) * channels * height * width +
+        static_cast<long long>(pr) * patch * width;
+    Out* const out = patches + (static_cast<long long>(image) * patch_rows * across +
+                                static_cast<long long>(pr) * across) * row_length;
+    for (int i = threadIdx.x; i < count; i += kThreads) {
+        const int channel = i / per_channel;
+        const int rest = i - channel * per_channel;
+        const int r = rest / quads;
+        const int column = (rest - r * quads) * 4;
+        const int pc = column / patch;
+        const int q = column - pc * patch;
+        const float4 value = __ldg(reinterpret_cast<const float4*>(
+            base + static_cast<long long>(channel) * height * width +
+            static_cast<long long>(r) * width + column));
+        store4(out + pc * row_length + channel * area + r * patch + q, value);
+    }
+}
+
 // Grid for a grid-stride loop over count items, or -1 when the reference would have
 // exceeded the CUDA grid limit (src/kernels/normalization.cu:214-220).
 long long elementwise_grid(long long count) {
@@ -553,9 +592,15 @@ int extract_patches_impl(const float* images, void* patches, int out_dtype, int 
     const bool vec = patch % 4 == 0 && width % 4 == 0 && aligned(images, 16) &&
                      aligned(patches, bf16 ? 8 : 16);
     const unsigned blocks = static_cast<unsigned>(grid);
+    const long long strips = static_cast<long long>(batch) * (height / patch);
+    const bool by_rows = vec && strips <= 0x7FFFFFFFLL;
     const auto run = [&](auto* out) {
         using Out = std::remove_pointer_t<decltype(out)>;
-        if (vec) {
+        if (by_rows) {
+            host::pdl_launch(extract_patch_rows_kernel<Out>, static_cast<unsigned>(strips),
+                             kThreads, 0, stream, images, out, channels, height, width, patch,
+                             across, height / patch, host::reverse_sweep() ? 1 : 0);
+        } else if (vec) {
             host::pdl_launch(extract_patches_kernel<Out, 4>, blocks, kThreads, 0, stream,
                              images, out, channels, height, width, patch, across, per_image,
                              total);
