@@ -211,7 +211,7 @@ def our_arm(args) -> None:
     import torch.distributed as dist
 
     import cuvit
-    from cuvit.replicas import gather_logits
+    from cuvit.replicas import bind_to_gpu_cpus, gather_logits
     from cuvit.vit import (PRECISION_BF16, PRECISION_TF32, VisionTransformer, VitConfig,
                            random_weights)
 
@@ -221,6 +221,9 @@ def our_arm(args) -> None:
     torch.cuda.set_device(local_rank)
     device = torch.device("cuda", local_rank)
     if world > 1:
+        # Each rank on its GPU's NUMA node, so its pinned images feed the copy engine from
+        # local memory (N = 1 keeps every core: the CPU baseline runs there).
+        bind_to_gpu_cpus(local_rank)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
                                 device_id=device)
 

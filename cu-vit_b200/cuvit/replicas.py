@@ -7,6 +7,52 @@ The helpers work on any torch.distributed backend (NCCL on GPUs, gloo on CPU for
 
 from __future__ import annotations
 
+import os
+
+SYSFS_PCI_DEVICES = "/sys/bus/pci/devices"
+
+
+def parse_cpulist(text: str) -> list[int]:
+    """CPUs of a Linux cpulist string ("0-7,16-23", "3", "")."""
+    cpus: list[int] = []
+    for part in text.strip().split(","):
+        if not part:
+            continue
+        first, _, last = part.partition("-")
+        cpus.extend(range(int(first), int(last or first) + 1))
+    return cpus
+
+
+def device_local_cpus(domain: int, bus: int, device: int,
+                      root: str = SYSFS_PCI_DEVICES) -> list[int] | None:
+    """The CPUs Linux lists as local to a PCI device (its NUMA node's cores), or None where
+    sysfs has no such entry."""
+    path = os.path.join(root, f"{domain:04x}:{bus:02x}:{device:02x}.0", "local_cpulist")
+    try:
+        with open(path) as handle:
+            return parse_cpulist(handle.read())
+    except (OSError, ValueError):
+        return None
+
+
+def bind_to_gpu_cpus(gpu: int, root: str = SYSFS_PCI_DEVICES) -> list[int] | None:
+    """Restricts the calling process to the CPUs local to CUDA device `gpu` (kept within the
+    CPUs it may already use), so host memory it allocates afterwards -- pinned staging
+    buffers above all -- sits on the GPU's NUMA node and host-device copies avoid the
+    socket interconnect. Returns the CPUs bound, or None (nothing changed) where the
+    topology is unknown or shares no CPU with the current affinity."""
+    import torch
+
+    props = torch.cuda.get_device_properties(gpu)
+    local = device_local_cpus(props.pci_domain_id, props.pci_bus_id, props.pci_device_id, root)
+    if not local:
+        return None
+    allowed = sorted(set(local) & os.sched_getaffinity(0))
+    if not allowed:
+        return None
+    os.sched_setaffinity(0, allowed)
+    return allowed
+
 
 def shard(total: int, world: int, rank: int) -> tuple[int, int]:
     """Contiguous slice [start, start + count) of `total` images owned by `rank`; the first

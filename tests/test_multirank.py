@@ -97,6 +97,21 @@ def test_shard_covers_the_batch_in_order():
         shard(8, 2, 2)
 
 
+def test_cpu_lists_and_device_locality_from_sysfs(tmp_path):
+    """Each rank binds to its GPU's NUMA-local CPUs (bench.py, N > 1); the topology comes from
+    the PCI device's local_cpulist in sysfs, here a fake tree."""
+    from cuvit.replicas import device_local_cpus, parse_cpulist
+
+    assert parse_cpulist("0-3,8,10-11\n") == [0, 1, 2, 3, 8, 10, 11]
+    assert parse_cpulist("") == []
+    entry = tmp_path / "0000:1b:00.0"
+    entry.mkdir()
+    (entry / "local_cpulist").write_text("56-111,168-223\n")
+    cpus = device_local_cpus(0, 0x1B, 0, root=str(tmp_path))
+    assert cpus[0] == 56 and cpus[-1] == 223 and len(cpus) == 112
+    assert device_local_cpus(0, 0x2C, 0, root=str(tmp_path)) is None
+
+
 @pytest.mark.parametrize("world,total", [(2, 6), (3, 7)])
 def test_gathered_logits_equal_one_whole_batch(world, total):
     results = _run(world, total, "ok")
