@@ -3,6 +3,8 @@
 // path (128-bit loads, one warp per row for the row reductions, values held in registers so
 // a row is read from HBM once) and a general path for shapes or alignments it cannot take.
 // Validation follows the reference launchers in src/kernels/normalization.cu:224-350.
+#include "elementwise.hpp"
+
 #include "cuvit_b200.h"
 #include "ptx.cuh"
 #include "runtime.hpp"
@@ -435,10 +437,11 @@ __global__ void extract_patches_kernel(const float* __restrict__ images, Out* __
 // The same gather, one block per (image, row of patches): the block reads that strip of the
 // image (channels x patch rows x width) with coalesced 16-byte loads along image rows and
 // writes each 4-value group to its patch, so consecutive threads write consecutive 4-value
-// groups of a patch row. Needs patch and width multiples of 4.
-template <typename Out>
+// groups of a patch row. Needs patch and width multiples of 4. In = __nv_bfloat16 (images the
+// host already rounded, with Out = __nv_bfloat16) moves 4 values as 8 bytes unchanged.
+template <typename In, typename Out>
 __global__ void __launch_bounds__(kThreads)
-    extract_patch_rows_kernel(const float* __restrict__ images, Out* __restrict__ patches,
+    extract_patch_rows_kernel(const In* __restrict__ images, Out* __restrict__ patches,
                               int channels, int height, int width, int patch, int across,
                               int patch_rows, int reverse) {
     dev::grid_dependency_wait();
@@ -452,9 +455,8 @@ __global__ void __launch_bounds__(kThreads)
     const int count = channels * per_channel;   // float4 in the strip
     const int area = patch * patch;
     const long long row_length = static_cast<long long>(channels) * area;
-    const float* const base =
-        images + static_cast<long long>(image) * channels * height * width +
-        static_cast<long long>(pr) * patch * width;
+    const In* const base = images + static_cast<long long>(image) * channels * height * width +
+                           static_cast<long long>(pr) * patch * width;
     Out* const out = patches + (static_cast<long long>(image) * patch_rows * across +
                                 static_cast<long long>(pr) * across) * row_length;
     for (int i = threadIdx.x; i < count; i += kThreads) {
@@ -464,10 +466,15 @@ __global__ void __launch_bounds__(kThreads)
         const int column = (rest - r * quads) * 4;
         const int pc = column / patch;
         const int q = column - pc * patch;
-        const float4 value = __ldg(reinterpret_cast<const float4*>(
-            base + static_cast<long long>(channel) * height * width +
-            static_cast<long long>(r) * width + column));
-        store4(out + pc * row_length + channel * area + r * patch + q, value);
+        const In* const source = base + static_cast<long long>(channel) * height * width +
+                                 static_cast<long long>(r) * width + column;
+        Out* const target = out + pc * row_length + channel * area + r * patch + q;
+        if constexpr (std::is_same_v<In, float>) {
+            store4(target, __ldg(reinterpret_cast<const float4*>(source)));
+        } else {
+            static_assert(std::is_same_v<Out, __nv_bfloat16>, "bfloat16 images give bfloat16");
+            *reinterpret_cast<uint2*>(target) = __ldg(reinterpret_cast<const uint2*>(source));
+        }
     }
 }
 
@@ -597,7 +604,7 @@ int extract_patches_impl(const float* images, void* patches, int out_dtype, int 
     const auto run = [&](auto* out) {
         using Out = std::remove_pointer_t<decltype(out)>;
         if (by_rows) {
-            host::pdl_launch(extract_patch_rows_kernel<Out>, static_cast<unsigned>(strips),
+            host::pdl_launch(extract_patch_rows_kernel<float, Out>, static_cast<unsigned>(strips),
                              kThreads, 0, stream, images, out, channels, height, width, patch,
                              across, height / patch, host::reverse_sweep() ? 1 : 0);
         } else if (vec) {
@@ -621,6 +628,34 @@ int extract_patches_impl(const float* images, void* patches, int out_dtype, int 
 }
 
 } // namespace
+
+bool bf16_patch_gather_supported(int height, int width, int patch) {
+    return patch > 0 && patch % 4 == 0 && width % 4 == 0 && height % patch == 0 &&
+           width % patch == 0;
+}
+
+int extract_patches_bf16(const __nv_bfloat16* images, __nv_bfloat16* patches, int batch,
+                         int channels, int height, int width, int patch, cudaStream_t stream) {
+    if (batch == 0) {
+        return CUVIT_OK;
+    }
+    if (batch < 0 || channels <= 0 || !bf16_patch_gather_supported(height, width, patch) ||
+        !aligned(images, 8) || !aligned(patches, 8)) {
+        return host::fail(CUVIT_INVALID_ARGUMENT,
+                          "bfloat16 patch gather needs whole patches, patch and width multiples "
+                          "of 4 and 8-byte aligned buffers");
+    }
+    const long long strips = static_cast<long long>(batch) * (height / patch);
+    if (strips > 0x7FFFFFFFLL) {
+        return host::fail(CUVIT_LENGTH_ERROR, "Elementwise launch exceeds the CUDA grid limit");
+    }
+    host::pdl_launch(extract_patch_rows_kernel<__nv_bfloat16, __nv_bfloat16>,
+                     static_cast<unsigned>(strips), kThreads, 0, stream, images, patches,
+                     channels, height, width, patch, width / patch, height / patch,
+                     host::reverse_sweep() ? 1 : 0);
+    return host::after_launch("extract_patches");
+}
+
 } // namespace cuvit::ops
 
 using cuvit::host::fail;

@@ -11,19 +11,26 @@
 // reference's own three steps (scaled Q.K^T GEMM, row softmax, P.V GEMM) on 3xTF32 GEMMs.
 // The residual stream (tokens) is FP32 in every precision.
 #include "cuvit_b200.h"
+#include "elementwise.hpp"
 #include "gemm.hpp"
 #include "runtime.hpp"
 
 #include <cuda_runtime.h>
+#include <sched.h>
 
+#include <algorithm>
 #include <cmath>
+#include <condition_variable>
 #include <cstdint>
 #include <cstdio>
 #include <cstring>
 #include <fstream>
+#include <functional>
 #include <map>
 #include <memory>
+#include <mutex>
 #include <string>
+#include <thread>
 #include <tuple>
 #include <unordered_map>
 #include <vector>
@@ -91,6 +98,103 @@ std::string shape_string(const std::vector<int64_t>& extents) {
 constexpr size_t kArenaAlignment = 256;
 
 size_t align_up(size_t bytes) { return (bytes + kArenaAlignment - 1) / kArenaAlignment * kArenaAlignment; }
+
+// A fixed set of host threads that split one job: run(job) calls job(part, parts) once per part
+// (the calling thread takes part 0) and returns when every part is done.
+class HostPool {
+  public:
+    explicit HostPool(int threads) : parts_(threads < 1 ? 1 : threads) {
+        for (int i = 1; i < parts_; ++i) {
+            workers_.emplace_back([this, i] { work(i); });
+        }
+    }
+    ~HostPool() {
+        {
+            std::lock_guard<std::mutex> lock(mutex_);
+            stop_ = true;
+        }
+        start_.notify_all();
+        for (std::thread& worker : workers_) {
+            worker.join();
+        }
+    }
+    HostPool(const HostPool&) = delete;
+    HostPool& operator=(const HostPool&) = delete;
+
+    int parts() const { return parts_; }
+
+    void run(const std::function<void(int, int)>& job) {
+        {
+            std::lock_guard<std::mutex> lock(mutex_);
+            job_ = &job;
+            pending_ = parts_ - 1;
+            ++generation_;
+        }
+        start_.notify_all();
+        job(0, parts_);
+        std::unique_lock<std::mutex> lock(mutex_);
+        done_.wait(lock, [this] { return pending_ == 0; });
+        job_ = nullptr;
+    }
+
+  private:
+    void work(int part) {
+        uint64_t seen = 0;
+        for (;;) {
+            const std::function<void(int, int)>* job = nullptr;
+            {
+                std::unique_lock<std::mutex> lock(mutex_);
+                start_.wait(lock, [&] { return stop_ || generation_ != seen; });
+                if (stop_) {
+                    return;
+                }
+                seen = generation_;
+                job = job_;
+            }
+            (*job)(part, parts_);
+            {
+                std::lock_guard<std::mutex> lock(mutex_);
+                if (--pending_ == 0) {
+                    done_.notify_one();
+                }
+            }
+        }
+    }
+
+    const int parts_;
+    std::vector<std::thread> workers_;
+    std::mutex mutex_;
+    std::condition_variable start_;
+    std::condition_variable done_;
+    const std::function<void(int, int)>* job_ = nullptr;
+    uint64_t generation_ = 0;
+    int pending_ = 0;
+    bool stop_ = false;
+};
+
+// Host threads for rounding images: the CPUs this process may run on, at most 8 (the
+// conversion is bound by host memory bandwidth well before that).
+int host_threads() {
+    cpu_set_t set;
+    CPU_ZERO(&set);
+    int cpus = 1;
+    if (sched_getaffinity(0, sizeof(set), &set) == 0) {
+        cpus = CPU_COUNT(&set);
+    }
+    return std::clamp(cpus, 1, 8);
+}
+
+// count floats -> bfloat16 bit patterns, rounded to nearest even (quiet NaN kept): the
+// rounding the BF16 path's patch gather applies to every pixel on the device.
+void round_to_bf16(const float* in, uint16_t* out, size_t count) {
+    for (size_t i = 0; i < count; ++i) {
+        uint32_t u = 0;
+        std::memcpy(&u, in + i, sizeof(u));
+        const uint32_t rounded = (u + 0x7FFFU + ((u >> 16) & 1U)) >> 16;
+        const uint32_t nan = (u >> 16) | 0x40U;
+        out[i] = static_cast<uint16_t>((u & 0x7FFFFFFFU) > 0x7F800000U ? nan : rounded);
+    }
+}
 
 // Restores the caller's current device on scope exit.
 class DeviceGuard {
@@ -160,7 +264,8 @@ struct cuvit_vit {
     float* stage_logits = nullptr;
 
     cudaStream_t capture_stream = nullptr;
-    std::map<std::tuple<int, const float*, float*>, cudaGraphExec_t> graphs;
+    // (batch, images, logits, images are bfloat16) -> the captured pass
+    std::map<std::tuple<int, const void*, float*, bool>, cudaGraphExec_t> graphs;
 
     // forward_host: images per chunk (0 = automatic), the stream that carries the
     // host-to-device copies, and one event per chunk marking its copy complete.
@@ -174,6 +279,13 @@ struct cuvit_vit {
     int async_slot = 0;
     cudaEvent_t slot_loaded[2] = {nullptr, nullptr};
     cudaEvent_t slot_free[2] = {nullptr, nullptr};
+
+    // BF16 path: forward_host_async rounds the host images to bfloat16 on the host (the
+    // rounding the device's patch gather would apply) into pinned slots, halving the bytes that
+    // cross PCIe; the device slot then holds bfloat16 images.
+    bool host_bf16 = false;
+    uint16_t* pinned_bf16[2] = {nullptr, nullptr};
+    std::unique_ptr<cuvit::model::HostPool> pool;
 };
 
 namespace cuvit::model {
@@ -373,8 +485,9 @@ int run_block(cuvit_vit& m, const BlockWeights& w, int layer, int batch, cudaStr
     return CUVIT_OK;
 }
 
-int run_forward(cuvit_vit& m, const float* images, float* logits, int batch, cudaStream_t stream,
-                Recorder* recorder = nullptr) {
+// images: planar FP32 images, or (bf16_images) the same rounded to bfloat16 by the host.
+int run_forward(cuvit_vit& m, const void* images, float* logits, int batch, cudaStream_t stream,
+                Recorder* recorder = nullptr, bool bf16_images = false) {
     const cuvit_vit_config& c = m.config;
     const int side = c.image_size / c.patch_size;
     const int patch_count = side * side;
@@ -387,10 +500,18 @@ int run_forward(cuvit_vit& m, const float* images, float* logits, int batch, cud
     const cuvit_stream_t s = reinterpret_cast<cuvit_stream_t>(stream);
     bool reverse = false;
 
-    CUVIT_LAUNCH(CUVIT_KIND_PATCHES, -1, 0.0,
-                 b * patch_count * patch_elements * (4 + es),
-                 cuvit_extract_patches_ex(images, m.patches, dtype, batch, c.channels,
-                                          c.image_size, c.image_size, c.patch_size, s));
+    if (bf16_images) {
+        CUVIT_LAUNCH(CUVIT_KIND_PATCHES, -1, 0.0, b * patch_count * patch_elements * (2 + es),
+                     cuvit::ops::extract_patches_bf16(
+                         static_cast<const __nv_bfloat16*>(images),
+                         static_cast<__nv_bfloat16*>(m.patches), batch, c.channels,
+                         c.image_size, c.image_size, c.patch_size, stream));
+    } else {
+        CUVIT_LAUNCH(CUVIT_KIND_PATCHES, -1, 0.0, b * patch_count * patch_elements * (4 + es),
+                     cuvit_extract_patches_ex(static_cast<const float*>(images), m.patches,
+                                              dtype, batch, c.channels, c.image_size,
+                                              c.image_size, c.patch_size, s));
+    }
     // Class token + positional embedding first; the patch-embedding GEMM then accumulates
     // into rows 1..T-1 (the reference writes the GEMM first and adds after, vit.cu:290-300;
     // each element sees the same two roundings).
@@ -582,10 +703,29 @@ int build(cuvit_vit* m, const float* const* host) {
         CUVIT_TRY_CUDA(cudaEventCreateWithFlags(&m->slot_loaded[slot], cudaEventDisableTiming));
         CUVIT_TRY_CUDA(cudaEventCreateWithFlags(&m->slot_free[slot], cudaEventDisableTiming));
     }
+    m->host_bf16 = m->precision == CUVIT_MATH_BF16 &&
+                   cuvit::ops::bf16_patch_gather_supported(c.image_size, c.image_size,
+                                                           c.patch_size);
+    if (m->host_bf16) {
+        const size_t pinned_bytes = static_cast<size_t>(images) * c.channels * c.image_size *
+                                    c.image_size * sizeof(uint16_t);
+        for (int slot = 0; slot < 2; ++slot) {
+            CUVIT_TRY_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&m->pinned_bf16[slot]),
+                                         pinned_bytes, cudaHostAllocDefault));
+        }
+        m->pool = std::make_unique<HostPool>(host_threads());
+    }
     return CUVIT_OK;
 }
 
 void release(cuvit_vit* m) {
+    m->pool.reset();
+    for (int slot = 0; slot < 2; ++slot) {
+        if (m->pinned_bf16[slot] != nullptr) {
+            cudaFreeHost(m->pinned_bf16[slot]);
+            m->pinned_bf16[slot] = nullptr;
+        }
+    }
     for (auto& entry : m->graphs) {
         cudaGraphExecDestroy(entry.second);
     }
@@ -771,9 +911,9 @@ int create(const cuvit_vit_config* config, const float* const* tensors, int max_
 // The executable graph of one whole pass for (batch, images, logits), captured on first use.
 // Work already queued on `stream` uses the same activation buffers, so the eager warm-up
 // pass and the capture start only after it.
-int graph_for(cuvit_vit& m, const float* images, float* logits, int batch, cudaStream_t stream,
-              cudaGraphExec_t* exec) {
-    const auto key = std::make_tuple(batch, images, logits);
+int graph_for(cuvit_vit& m, const void* images, float* logits, int batch, cudaStream_t stream,
+              cudaGraphExec_t* exec, bool bf16_images = false) {
+    const auto key = std::make_tuple(batch, images, logits, bf16_images);
     auto found = m.graphs.find(key);
     if (found == m.graphs.end()) {
         CUVIT_TRY_CUDA(cudaEventRecord(m.entry_event, stream));
@@ -781,13 +921,14 @@ int graph_for(cuvit_vit& m, const float* images, float* logits, int batch, cudaS
         // One eager pass first, so every one-time set-up (device context, kernel attributes,
         // the driver's tensor-map entry point) happens outside the capture, where device
         // synchronisation is allowed.
-        CUVIT_TRY(run_forward(m, images, logits, batch, m.capture_stream));
+        CUVIT_TRY(run_forward(m, images, logits, batch, m.capture_stream, nullptr, bf16_images));
         CUVIT_TRY_CUDA(cudaStreamSynchronize(m.capture_stream));
         // Capture on the model's own stream: the caller's may be the legacy default stream,
         // which cannot be captured.
         CUVIT_TRY_CUDA(
             cudaStreamBeginCapture(m.capture_stream, cudaStreamCaptureModeThreadLocal));
-        const int status = run_forward(m, images, logits, batch, m.capture_stream);
+        const int status =
+            run_forward(m, images, logits, batch, m.capture_stream, nullptr, bf16_images);
         cudaGraph_t graph = nullptr;
         const cudaError_t end = cudaStreamEndCapture(m.capture_stream, &graph);
         CUVIT_TRY(status);
@@ -1009,16 +1150,38 @@ int cuvit_vit_forward_host_async(cuvit_vit* model, const float* images, float* l
     const cuvit_vit_config& c = model->config;
     const int slot = model->async_slot;
     float* const staged = slot == 0 ? model->stage_images : model->stage_images_alt;
+    const bool bf16 = model->host_bf16;
     cudaGraphExec_t exec = nullptr;
-    CUVIT_TRY(graph_for(*model, staged, model->stage_logits, batch, s, &exec));
+    CUVIT_TRY(graph_for(*model, staged, model->stage_logits, batch, s, &exec, bf16));
     model->async_slot = slot ^ 1;
-    // The copy waits only for the pass that last read this slot (two calls back), so it
-    // overlaps the pass of the previous call; the pass waits for the copy.
-    const size_t image_bytes =
-        static_cast<size_t>(batch) * c.channels * c.image_size * c.image_size * sizeof(float);
+    const size_t count = static_cast<size_t>(batch) * c.channels * c.image_size * c.image_size;
+    // The copies wait only for the pass that last read this slot (two calls back), so they
+    // overlap the pass of the previous call; the pass waits for the copies.
     CUVIT_TRY_CUDA(cudaStreamWaitEvent(model->copy_stream, model->slot_free[slot], 0));
-    CUVIT_TRY_CUDA(
-        cudaMemcpyAsync(staged, images, image_bytes, cudaMemcpyHostToDevice, model->copy_stream));
+    if (bf16) {
+        // Round the images into this slot's pinned buffer, once the copy that last read it
+        // (two calls back) has finished; meanwhile the device runs the previous call's pass.
+        // Quarter by quarter, so each quarter's copy overlaps the rounding of the next.
+        CUVIT_TRY_CUDA(cudaEventSynchronize(model->slot_loaded[slot]));
+        uint16_t* const pinned = model->pinned_bf16[slot];
+        uint16_t* const device = reinterpret_cast<uint16_t*>(staged);
+        constexpr int kPieces = 4;
+        for (int piece = 0; piece < kPieces; ++piece) {
+            const size_t first = count * piece / kPieces;
+            const size_t last = count * (piece + 1) / kPieces;
+            model->pool->run([&](int part, int parts) {
+                const size_t begin = first + (last - first) * part / parts;
+                const size_t end = first + (last - first) * (part + 1) / parts;
+                cuvit::model::round_to_bf16(images + begin, pinned + begin, end - begin);
+            });
+            CUVIT_TRY_CUDA(cudaMemcpyAsync(device + first, pinned + first,
+                                           (last - first) * sizeof(uint16_t),
+                                           cudaMemcpyHostToDevice, model->copy_stream));
+        }
+    } else {
+        CUVIT_TRY_CUDA(cudaMemcpyAsync(staged, images, count * sizeof(float),
+                                       cudaMemcpyHostToDevice, model->copy_stream));
+    }
     CUVIT_TRY_CUDA(cudaEventRecord(model->slot_loaded[slot], model->copy_stream));
     CUVIT_TRY_CUDA(cudaStreamWaitEvent(s, model->slot_loaded[slot], 0));
     CUVIT_TRY_CUDA(cudaGraphLaunch(exec, s));
@@ -1083,6 +1246,9 @@ size_t cuvit_vit_image_elements(const cuvit_vit* model) {
     }
     return static_cast<size_t>(model->config.channels) * model->config.image_size *
            model->config.image_size;
+}
+size_t cuvit_vit_host_image_bytes(const cuvit_vit* model) {
+    return cuvit_vit_image_elements(model) * (model != nullptr && model->host_bf16 ? 2 : 4);
 }
 
 int cuvit_vit_launches_per_forward(const cuvit_vit* model, int batch) {

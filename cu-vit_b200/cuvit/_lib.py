@@ -150,6 +150,7 @@ SIGNATURES = {
     "cuvit_vit_weight_bytes": (_sz, [_vp]),
     "cuvit_vit_activation_bytes": (_sz, [_vp]),
     "cuvit_vit_image_elements": (_sz, [_vp]),
+    "cuvit_vit_host_image_bytes": (_sz, [_vp]),
     "cuvit_vit_launches_per_forward": (_i, [_vp, _i]),
 }
 

@@ -242,6 +242,11 @@ class VisionTransformer:
     def image_elements(self) -> int:
         return int(_lib.library().cuvit_vit_image_elements(self._handle))
 
+    def host_image_bytes(self) -> int:
+        """Bytes per image that forward_host_async moves host -> device (2 per element where
+        the model rounds images to bfloat16 on the host, else 4)."""
+        return int(_lib.library().cuvit_vit_host_image_bytes(self._handle))
+
     def weight_bytes(self) -> int:
         return int(_lib.library().cuvit_vit_weight_bytes(self._handle))
 

@@ -150,7 +150,24 @@ def test_async_host_calls_pipeline_correctly(cuda):
     assert per_image * 6 == pinned_in[0].numel()
     # The synchronous path after asynchronous calls still sees its own images.
     np.testing.assert_array_equal(model.forward_host(inputs[2]), want[2])
+    # BF16 models round the images on the host, so pageable inputs serve as well; the images
+    # may change as soon as the call returns.
+    pageable = np.ascontiguousarray(inputs[0])
+    out = cuda.full((6, config.classes), float("nan")).pin_memory()
+    model.forward_host_async(pageable.ctypes.data, out.data_ptr(), 6, stream)
+    pageable[:] = 0.0
+    stream.synchronize()
+    np.testing.assert_array_equal(out.numpy(), want[0])
     model.close()
+    # FP32 models copy the FP32 images as they are.
+    fp32 = VisionTransformer(config, weights, max_batch=6, precision=PRECISION_FP32)
+    eager = model_logits(fp32, inputs[1], 6, cuda)
+    fp32_out = cuda.full((6, config.classes), float("nan")).pin_memory()
+    for _ in range(3):
+        fp32.forward_host_async(pinned_in[1].data_ptr(), fp32_out.data_ptr(), 6, stream)
+    stream.synchronize()
+    np.testing.assert_array_equal(fp32_out.numpy(), eager)
+    fp32.close()
 
 
 def test_graph_capture_waits_for_queued_work(cuda):
