@@ -172,16 +172,30 @@ class HostPool {
     bool stop_ = false;
 };
 
-// Host threads for rounding images: the CPUs this process may run on, at most 8 (the
-// conversion is bound by host memory bandwidth well before that).
-int host_threads() {
+// CPUs this process may run on.
+int process_cpus() {
     cpu_set_t set;
     CPU_ZERO(&set);
-    int cpus = 1;
     if (sched_getaffinity(0, sizeof(set), &set) == 0) {
-        cpus = CPU_COUNT(&set);
+        return CPU_COUNT(&set);
     }
-    return std::clamp(cpus, 1, 8);
+    return 1;
+}
+
+// Host threads for rounding images: the process's CPUs, at most 8 (the conversion is bound
+// by host memory bandwidth well before that).
+int host_threads() { return std::clamp(process_cpus(), 1, 8); }
+
+// Whether forward_host_async rounds images to bfloat16 on the host: only with
+// CUVIT_HOST_ROUNDING=1. It halves the bytes that cross PCIe but costs ~28 ms of one core per
+// 256 ViT images and 1.5x the image bytes in host memory traffic (read 4, write 2, copy 2 per
+// pixel, against 4 for copying FP32): on the B200 hosts measured, the FP32 copy already hides
+// under the pass (e2e 98% of device-timed at 1, 2 and 8 GPUs) and rounding gained nothing at
+// 2 GPUs per host and lost a third of e2e at 8 (8 GPUs sharing 32 CPUs). For PCIe-limited
+// hosts with cores to spare.
+bool host_rounding_enabled() {
+    const char* value = std::getenv("CUVIT_HOST_ROUNDING");
+    return value != nullptr && std::strcmp(value, "1") == 0;
 }
 
 // count floats -> bfloat16 bit patterns, rounded to nearest even (quiet NaN kept): the
@@ -703,7 +717,7 @@ int build(cuvit_vit* m, const float* const* host) {
         CUVIT_TRY_CUDA(cudaEventCreateWithFlags(&m->slot_loaded[slot], cudaEventDisableTiming));
         CUVIT_TRY_CUDA(cudaEventCreateWithFlags(&m->slot_free[slot], cudaEventDisableTiming));
     }
-    m->host_bf16 = m->precision == CUVIT_MATH_BF16 &&
+    m->host_bf16 = m->precision == CUVIT_MATH_BF16 && host_rounding_enabled() &&
                    cuvit::ops::bf16_patch_gather_supported(c.image_size, c.image_size,
                                                            c.patch_size);
     if (m->host_bf16) {

@@ -35,23 +35,42 @@ def device_local_cpus(domain: int, bus: int, device: int,
         return None
 
 
+def cpu_share(gpu: int, local: dict[int, list[int]], allowed: set[int]) -> list[int]:
+    """This GPU's CPUs: those local to it (and allowed), split evenly in device order among
+    the GPUs with the same local CPUs, so one process per GPU gets a disjoint share."""
+    mine = sorted(set(local[gpu]) & allowed)
+    peers = [g for g in sorted(local) if local[g] == local[gpu]]
+    if len(peers) > 1 and mine:
+        index = peers.index(gpu)
+        share = mine[index * len(mine) // len(peers):(index + 1) * len(mine) // len(peers)]
+        if share:
+            return share
+    return mine
+
+
 def bind_to_gpu_cpus(gpu: int, root: str = SYSFS_PCI_DEVICES) -> list[int] | None:
-    """Restricts the calling process to the CPUs local to CUDA device `gpu` (kept within the
-    CPUs it may already use), so host memory it allocates afterwards -- pinned staging
-    buffers above all -- sits on the GPU's NUMA node and host-device copies avoid the
-    socket interconnect. Returns the CPUs bound, or None (nothing changed) where the
-    topology is unknown or shares no CPU with the current affinity."""
+    """Restricts the calling process to its share of the CPUs local to CUDA device `gpu`
+    (cpu_share, within the CPUs it may already use), so host memory it allocates afterwards
+    -- pinned staging buffers above all -- sits on the GPU's NUMA node, and host threads of
+    the processes of GPUs on one node (the BF16 model's image rounding) do not contend for
+    the same cores. Returns the CPUs bound, or None (nothing changed) where the topology is
+    unknown or shares no CPU with the current affinity."""
     import torch
 
-    props = torch.cuda.get_device_properties(gpu)
-    local = device_local_cpus(props.pci_domain_id, props.pci_bus_id, props.pci_device_id, root)
-    if not local:
+    local: dict[int, list[int]] = {}
+    for device in range(torch.cuda.device_count()):
+        props = torch.cuda.get_device_properties(device)
+        cpus = device_local_cpus(props.pci_domain_id, props.pci_bus_id, props.pci_device_id,
+                                 root)
+        if cpus:
+            local[device] = cpus
+    if gpu not in local:
         return None
-    allowed = sorted(set(local) & os.sched_getaffinity(0))
-    if not allowed:
+    share = cpu_share(gpu, local, os.sched_getaffinity(0))
+    if not share:
         return None
-    os.sched_setaffinity(0, allowed)
-    return allowed
+    os.sched_setaffinity(0, share)
+    return share
 
 
 def shard(total: int, world: int, rank: int) -> tuple[int, int]:

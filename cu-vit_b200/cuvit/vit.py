@@ -243,8 +243,9 @@ class VisionTransformer:
         return int(_lib.library().cuvit_vit_image_elements(self._handle))
 
     def host_image_bytes(self) -> int:
-        """Bytes per image that forward_host_async moves host -> device (2 per element where
-        the model rounds images to bfloat16 on the host, else 4)."""
+        """Bytes per image that forward_host_async moves host -> device: 2 per element where
+        the model rounds images to bfloat16 on the host (BF16 models created with
+        CUVIT_HOST_ROUNDING=1), else 4."""
         return int(_lib.library().cuvit_vit_host_image_bytes(self._handle))
 
     def weight_bytes(self) -> int:

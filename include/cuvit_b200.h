@@ -294,11 +294,12 @@ int cuvit_vit_forward_host(cuvit_vit* model, const float* images, float* logits,
  * pass of call i. The host buffers must stay valid and unchanged until `stream` has reached
  * this call's work (synchronize it, or wait on an event recorded after the call); the images
  * must hold their data when the call is made, since the copy is not ordered after earlier
- * work on `stream`. Consecutive calls on one model must use the same stream. For BF16 models
- * (patch size and image width multiples of 4) the call first rounds the images to bfloat16
- * on host threads into pinned buffers the model owns -- the rounding the device would apply
- * to every pixel, so the logits are the same -- and copies half the bytes; the images are
- * then read before the call returns and need not be pinned. No reference counterpart (the
+ * work on `stream`. Consecutive calls on one model must use the same stream. BF16 models
+ * (patch size and image width multiples of 4) created with CUVIT_HOST_ROUNDING=1 in the
+ * environment first round the images to bfloat16 on host threads into pinned buffers the
+ * model owns -- the rounding the device would apply to every pixel, so the logits are the
+ * same -- and copy half the bytes (for hosts where PCIe, not host memory, limits the copy);
+ * the images are then read before the call returns. No reference counterpart (the
  * reference's host-vector forward is synchronous). */
 int cuvit_vit_forward_host_async(cuvit_vit* model, const float* images, float* logits,
                                  int batch, cuvit_stream_t stream);
@@ -342,9 +343,9 @@ int cuvit_vit_max_batch(const cuvit_vit* model);
 size_t cuvit_vit_weight_bytes(const cuvit_vit* model);
 size_t cuvit_vit_activation_bytes(const cuvit_vit* model);
 size_t cuvit_vit_image_elements(const cuvit_vit* model);
-/* Bytes one image takes on its way host -> device in forward_host_async: 2 where the model
- * rounds images to bfloat16 on the host (BF16 models whose patch size and image width are
- * multiples of 4), else 4, per image element. No reference counterpart. */
+/* Bytes one image takes on its way host -> device in forward_host_async: 2 per image element
+ * where the model rounds images to bfloat16 on the host (see forward_host_async), else 4.
+ * No reference counterpart. */
 size_t cuvit_vit_host_image_bytes(const cuvit_vit* model);
 /* Kernel launches one forward pass issues for this batch size. */
 int cuvit_vit_launches_per_forward(const cuvit_vit* model, int batch);

@@ -112,6 +112,21 @@ def test_cpu_lists_and_device_locality_from_sysfs(tmp_path):
     assert device_local_cpus(0, 0x2C, 0, root=str(tmp_path)) is None
 
 
+def test_gpus_on_one_node_take_disjoint_cpu_shares():
+    from cuvit.replicas import cpu_share
+
+    node0, node1 = list(range(0, 16)), list(range(16, 32))
+    local = {g: (node0 if g < 4 else node1) for g in range(8)}
+    shares = [cpu_share(g, local, set(range(32))) for g in range(8)]
+    assert shares[0] == [0, 1, 2, 3] and shares[3] == [12, 13, 14, 15]
+    assert shares[4] == [16, 17, 18, 19] and shares[7] == [28, 29, 30, 31]
+    assert len({c for share in shares for c in share}) == 32
+    # fewer allowed CPUs than GPUs: every GPU keeps at least the allowed local ones
+    assert cpu_share(1, local, {0, 1}) in ([0], [1], [0, 1])
+    # one GPU per node keeps the node
+    assert cpu_share(0, {0: node0, 1: node1}, set(range(32))) == node0
+
+
 @pytest.mark.parametrize("world,total", [(2, 6), (3, 7)])
 def test_gathered_logits_equal_one_whole_batch(world, total):
     results = _run(world, total, "ok")

@@ -129,12 +129,19 @@ def test_chunked_host_path_matches_eager(cuda):
     model.close()
 
 
-def test_async_host_calls_pipeline_correctly(cuda):
+@pytest.mark.parametrize("host_rounding", ["1", "0"], ids=["host-rounding", "fp32-copy"])
+def test_async_host_calls_pipeline_correctly(host_rounding, cuda, monkeypatch):
     """forward_host_async(): back-to-back calls on alternating staging slots, with batch
-    sizes that change between calls, each give the eager logits of their own images."""
+    sizes that change between calls, each give the eager logits of their own images --
+    bitwise, whether the BF16 model rounds the images on the host (CUVIT_HOST_ROUNDING=1) or
+    copies them as FP32 for the device to round."""
     _, config, _, std, _, _ = golden_case("vit hd64")
     weights = random_weights(config, 737, std=std)
+    monkeypatch.setenv("CUVIT_HOST_ROUNDING", host_rounding)
     model = VisionTransformer(config, weights, max_batch=6, precision=PRECISION_BF16)
+    monkeypatch.delenv("CUVIT_HOST_ROUNDING")
+    assert model.host_image_bytes() == config.image_elements() * (2 if host_rounding == "1"
+                                                                   else 4)
     per_image = config.image_elements()
     batches = [6, 6, 3, 6, 1, 5, 6]
     inputs = [mg.vit_images(config, b, 50 + i) for i, b in enumerate(batches)]
@@ -150,8 +157,8 @@ def test_async_host_calls_pipeline_correctly(cuda):
     assert per_image * 6 == pinned_in[0].numel()
     # The synchronous path after asynchronous calls still sees its own images.
     np.testing.assert_array_equal(model.forward_host(inputs[2]), want[2])
-    # BF16 models round the images on the host, so pageable inputs serve as well; the images
-    # may change as soon as the call returns.
+    # Pageable inputs serve as well; the images may change as soon as the call returns (the
+    # host rounding reads them inside the call, a pageable copy stages them before returning).
     pageable = np.ascontiguousarray(inputs[0])
     out = cuda.full((6, config.classes), float("nan")).pin_memory()
     model.forward_host_async(pageable.ctypes.data, out.data_ptr(), 6, stream)
