@@ -234,20 +234,6 @@ int choose_block_n(int n, bool split) {
 
 } // namespace
 
-int tc_smem_bytes(int elem_bytes, int block_n, bool split) {
-    if (split) {
-        return block_n == 64 ? TcShape<4, 64, true>::kSmemBytes : TcShape<4, 128, true>::kSmemBytes;
-    }
-    if (elem_bytes == 2) {
-        return block_n == 64    ? TcShape<2, 64, false>::kSmemBytes
-               : block_n == 128 ? TcShape<2, 128, false>::kSmemBytes
-                                : TcShape<2, 256, false>::kSmemBytes;
-    }
-    return block_n == 64    ? TcShape<4, 64, false>::kSmemBytes
-           : block_n == 128 ? TcShape<4, 128, false>::kSmemBytes
-                            : TcShape<4, 256, false>::kSmemBytes;
-}
-
 int resolve(const void* a, const void* b, const float* bias, void* c, int c_dtype, int math,
             const cuvit_gemm_problem& problem, Resolved* out, bool* empty) {
     *empty = false;

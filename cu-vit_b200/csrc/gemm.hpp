@@ -65,7 +65,5 @@ int launch_tc_pair(const Plan& plan, cudaStream_t stream);
 // CUVIT_GEMM_PAIRS=0 (which keeps every GEMM on the one-CTA kernel).
 bool pairs_enabled();
 
-// Dynamic shared memory the chosen instantiation needs.
-int tc_smem_bytes(int elem_bytes, int block_n, bool split);
 
 } // namespace cuvit::gemm
