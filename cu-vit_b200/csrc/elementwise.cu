@@ -478,6 +478,70 @@ __global__ void __launch_bounds__(kThreads)
     }
 }
 
+// Top-k report (report_top, src/main.cpp:90-114), one warp per row: the row maximum and sum
+// of exponentials, then k rounds of a warp-wide argmax over the entries that come after the
+// previous pick in (logit descending, index ascending) order.
+__global__ void __launch_bounds__(kThreads)
+    top_k_kernel(const float* __restrict__ logits, int batch, int classes, int k,
+                 int* __restrict__ indices, float* __restrict__ values,
+                 float* __restrict__ probabilities) {
+    dev::grid_dependency_wait();
+    dev::grid_launch_dependents();
+    const int row = blockIdx.x * kRowsPerBlock + threadIdx.x / kWarp;
+    const int lane = threadIdx.x % kWarp;
+    if (row >= batch) {
+        return;
+    }
+    const float* const x = logits + static_cast<long long>(row) * classes;
+    float maximum = -INFINITY;
+    for (int c = lane; c < classes; c += kWarp) {
+        maximum = fmaxf(maximum, __ldg(x + c));
+    }
+    maximum = warp_max(maximum);
+    float total = 0.0F;
+    for (int c = lane; c < classes; c += kWarp) {
+        total += expf(__ldg(x + c) - maximum);
+    }
+    total = warp_sum(total);
+    float last_value = INFINITY;
+    int last_index = -1;
+    const long long out = static_cast<long long>(row) * k;
+    for (int r = 0; r < k; ++r) {
+        float best_value = -INFINITY;
+        int best_index = -1;
+        for (int c = lane; c < classes; c += kWarp) {
+            const float v = __ldg(x + c);
+            const bool after = v < last_value || (v == last_value && c > last_index);
+            if (after && (best_index < 0 || v > best_value)) {
+                best_value = v;
+                best_index = c;
+            }
+        }
+#pragma unroll
+        for (int offset = 16; offset > 0; offset /= 2) {
+            const float other_value = __shfl_xor_sync(0xFFFFFFFFu, best_value, offset);
+            const int other_index = __shfl_xor_sync(0xFFFFFFFFu, best_index, offset);
+            const bool better =
+                other_index >= 0 &&
+                (best_index < 0 || other_value > best_value ||
+                 (other_value == best_value && other_index < best_index));
+            if (better) {
+                best_value = other_value;
+                best_index = other_index;
+            }
+        }
+        if (lane == 0) {
+            indices[out + r] = best_index;
+            values[out + r] = best_index < 0 ? NAN : best_value;
+            probabilities[out + r] = best_index < 0 ? 0.0F : expf(best_value - maximum) / total;
+        }
+        if (best_index >= 0) {
+            last_value = best_value;
+            last_index = best_index;
+        }
+    }
+}
+
 // Grid for a grid-stride loop over count items, or -1 when the reference would have
 // exceeded the CUDA grid limit (src/kernels/normalization.cu:214-220).
 long long elementwise_grid(long long count) {
@@ -848,6 +912,29 @@ int cuvit_round_to_tf32(const float* input, float* output, int64_t count,
     cuvit::host::pdl_launch(round_tf32_kernel, static_cast<unsigned>(grid), kThreads, 0,
                             reinterpret_cast<cudaStream_t>(stream), input, output, count);
     return cuvit::host::after_launch("round_to_tf32");
+}
+
+int cuvit_logits_top_k(const float* logits, int batch, int classes, int k, int* indices,
+                       float* values, float* probabilities, cuvit_stream_t stream) {
+    if (batch == 0) {
+        return CUVIT_OK;
+    }
+    if (batch < 0 || classes <= 0 || k < 1 || k > classes) {
+        return fail(CUVIT_INVALID_ARGUMENT,
+                    "top-k needs a non-negative batch, positive classes and 1 <= k <= classes");
+    }
+    if (logits == nullptr || indices == nullptr || values == nullptr ||
+        probabilities == nullptr) {
+        return fail(CUVIT_INVALID_ARGUMENT, "top-k operands cannot be null");
+    }
+    const long long blocks = (static_cast<long long>(batch) + kRowsPerBlock - 1) / kRowsPerBlock;
+    if (blocks > 0x7FFFFFFFLL) {
+        return fail(CUVIT_LENGTH_ERROR, "Elementwise launch exceeds the CUDA grid limit");
+    }
+    cuvit::host::pdl_launch(top_k_kernel, static_cast<unsigned>(blocks), kThreads, 0,
+                            reinterpret_cast<cudaStream_t>(stream), logits, batch, classes, k,
+                            indices, values, probabilities);
+    return cuvit::host::after_launch("top_k");
 }
 
 } // extern "C"

@@ -119,6 +119,7 @@ SIGNATURES = {
     "cuvit_init_tokens": (_i, [_vp, _vp, _vp, _i, _i, _i, _vp]),
     "cuvit_convert_f32_to_bf16": (_i, [_vp, _vp, _i64, _vp]),
     "cuvit_round_to_tf32": (_i, [_vp, _vp, _i64, _vp]),
+    "cuvit_logits_top_k": (_i, [_vp, _i, _i, _i, _vp, _vp, _vp, _vp]),
     "cuvit_attention": (_i, [_vp, _vp, _i, _i, _i, _i, _i, _f, _vp]),
     "cuvit_device_status": (_i, [ctypes.POINTER(ctypes.c_uint)]),
     "cuvit_launch_count": (ctypes.c_longlong, []),

@@ -198,6 +198,16 @@ def launch_round_to_tf32(input, output, count: int, stream=None) -> None:
                                              _stream(stream)))
 
 
+def launch_logits_top_k(logits, indices, values, probabilities, batch: int, classes: int,
+                        k: int, stream=None) -> None:
+    """reference: report_top (src/main.cpp:90-114) on the device: per row the k largest
+    logits (descending; equal logits by ascending class index) with their softmax
+    probabilities, into int32 / float32 / float32 arrays [batch, k]."""
+    check(_lib.library().cuvit_logits_top_k(_ptr(logits), batch, classes, k, _ptr(indices),
+                                            _ptr(values), _ptr(probabilities),
+                                            _stream(stream)))
+
+
 def launch_attention(qkv, context, dtype: int, batch: int, tokens: int, heads: int,
                      head_dim: int, scale: float, stream=None) -> None:
     """Fused Q.K^T -> softmax -> .V (replaces src/model/vit.cu:198-242)."""

@@ -207,6 +207,16 @@ int cuvit_convert_f32_to_bf16(const float* input, void* output, int64_t count,
 int cuvit_round_to_tf32(const float* input, float* output, int64_t count,
                         cuvit_stream_t stream);
 
+/* Top-k report of logits rows (reference: report_top, src/main.cpp:90-114, which the CLI runs
+ * on the host): for each of `batch` rows of `classes` device logits, the k largest in
+ * descending order -- equal logits by ascending class index, where the reference's
+ * partial_sort leaves their order open -- into device arrays [batch, k]: class indices,
+ * logits, and softmax probabilities exp(logit - max) / sum_j exp(logit_j - max). NaN logits
+ * are never reported; a row with fewer than k others reports index -1, value NaN and
+ * probability 0 in the remaining places. 1 <= k <= classes. */
+int cuvit_logits_top_k(const float* logits, int batch, int classes, int k, int* indices,
+                       float* values, float* probabilities, cuvit_stream_t stream);
+
 /* ---------------------------------------------------------------------------------------
  * Fused attention. Replaces the Q.K^T GEMM -> launch_softmax -> .V GEMM sequence of
  * src/model/vit.cu:198-242 with one kernel that keeps the T x T logits on chip.

@@ -53,6 +53,8 @@ def lib() -> ctypes.CDLL:
     library.oracle_layer_norm.argtypes = [ctypes.c_void_p, _i64, _f32p, _f32p, ctypes.c_void_p,
                                           _i64, _i, _i, _f]
     library.oracle_softmax.argtypes = [ctypes.c_void_p, ctypes.c_void_p, _i, _i, _i64]
+    library.oracle_top_k.argtypes = [_f32p, _i, _i, _i, ctypes.c_void_p, ctypes.c_void_p,
+                                     ctypes.c_void_p]
     library.oracle_gelu.restype = _f
     library.oracle_gelu.argtypes = [_f]
     library.oracle_gelu_array.argtypes = [_f32p, _f32p, _i64]
@@ -108,6 +110,19 @@ def softmax(x, rows, columns) -> np.ndarray:
     out = np.empty(rows * columns, np.float32)
     lib().oracle_softmax(x.ctypes.data, out.ctypes.data, rows, columns, columns)
     return out
+
+
+def top_k(logits, k: int):
+    """report_top (src/main.cpp:90-114) per row: (indices int32, logits float32,
+    probabilities float64), each [rows, k]; equal logits by ascending class index."""
+    logits = _f32(logits)
+    rows, classes = logits.shape
+    indices = np.empty((rows, k), np.int32)
+    values = np.empty((rows, k), np.float32)
+    probabilities = np.empty((rows, k), np.float64)
+    lib().oracle_top_k(logits.reshape(-1), rows, classes, k, indices.ctypes.data,
+                       values.ctypes.data, probabilities.ctypes.data)
+    return indices, values, probabilities
 
 
 def gelu(x) -> np.ndarray:

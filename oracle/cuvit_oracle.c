@@ -144,6 +144,44 @@ void oracle_softmax(const float* input, float* output, int rows, int columns, in
     }
 }
 
+/* Top-k report of logits rows: report_top, src/main.cpp:90-114. The k largest logits of each
+ * row in descending order (the reference's std::partial_sort leaves equal logits in no
+ * particular order; here the lower class index comes first) and their stable-softmax
+ * probabilities, exp(logit - max) / sum exp(logit_j - max), in double. */
+void oracle_top_k(const float* logits, int batch, int classes, int k, int* indices,
+                  float* values, double* probabilities) {
+    for (int row = 0; row < batch; ++row) {
+        const float* const x = logits + (int64_t)row * classes;
+        float maximum = x[0];
+        for (int c = 1; c < classes; ++c) {
+            maximum = x[c] > maximum ? x[c] : maximum;
+        }
+        double total = 0.0;
+        for (int c = 0; c < classes; ++c) {
+            total += exp((double)x[c] - maximum);
+        }
+        float last_value = INFINITY;
+        int last_index = -1;
+        for (int r = 0; r < k; ++r) {
+            int best = -1;
+            for (int c = 0; c < classes; ++c) {
+                const int after = x[c] < last_value || (x[c] == last_value && c > last_index);
+                if (after && (best < 0 || x[c] > x[best])) {
+                    best = c;
+                }
+            }
+            const int64_t out = (int64_t)row * k + r;
+            indices[out] = best;
+            values[out] = best < 0 ? NAN : x[best];
+            probabilities[out] = best < 0 ? 0.0 : exp((double)x[best] - maximum) / total;
+            if (best >= 0) {
+                last_value = x[best];
+                last_index = best;
+            }
+        }
+    }
+}
+
 /* Patch gather: src/kernels/normalization.cu:159-192, tests/reference/vit.hpp:67-87.
  * patches[b*P + p][ch*pp + r*patch + q] = images[b][ch][pr*patch + r][pc*patch + q]. */
 void oracle_extract_patches(const float* images, float* patches, int batch, int channels,

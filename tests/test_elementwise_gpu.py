@@ -202,6 +202,29 @@ def test_tf32_storage_outputs(cuda):
                                   tf32_round(oracle.extract_patches(images, 2, 3, 32, 32, 8)))
 
 
+@pytest.mark.parametrize("batch,classes,k", [(37, 1000, 5), (1, 1000, 1), (9, 33, 33),
+                                             (300, 10, 3)])
+def test_logits_top_k_matches_the_report(batch, classes, k, cuda):
+    """report_top (src/main.cpp:90-114) on the device: the same classes and logits as the
+    oracle, bitwise; probabilities within 1e-5 relative of its double-precision softmax."""
+    rng = np.random.default_rng(batch * 7 + classes)
+    logits = (3.0 * rng.standard_normal((batch, classes))).astype(np.float32)
+    logits[0, : min(4, classes)] = logits[0].max() + 1.0  # ties at the top
+    want_i, want_v, want_p = oracle.top_k(logits, k)
+    indices = cuda.zeros((batch, k), dtype=cuda.int32, device="cuda")
+    values = cuda.zeros((batch, k), device="cuda")
+    probabilities = cuda.zeros((batch, k), device="cuda")
+    kernels.launch_logits_top_k(to_device(logits), indices, values, probabilities, batch,
+                                classes, k)
+    cuda.cuda.synchronize()
+    np.testing.assert_array_equal(indices.cpu().numpy(), want_i)
+    np.testing.assert_array_equal(values.cpu().numpy(), want_v)
+    np.testing.assert_allclose(probabilities.cpu().numpy(), want_p, rtol=1e-5, atol=1e-30)
+    with pytest.raises(InvalidArgument):
+        kernels.launch_logits_top_k(to_device(logits), indices, values, probabilities, batch,
+                                    classes, classes + 1)
+
+
 def test_invalid_arguments_on_device_buffers(cuda):
     buffer = to_device(np.zeros(16))
     kernels.launch_gelu(buffer, buffer, 0)

@@ -97,6 +97,34 @@ def test_extract_patches_is_the_documented_gather(oracle_lib):
     np.testing.assert_array_equal(got.reshape(expected.shape), expected)
 
 
+def test_top_k_report_is_the_documented_selection(oracle_lib):
+    """report_top (src/main.cpp:90-114): the k largest logits per row in descending order
+    (equal logits by ascending class index) and softmax probabilities in double."""
+    rng = np.random.default_rng(9)
+    logits = rng.standard_normal((6, 1000)).astype(np.float32) * 3
+    logits[1, [10, 20, 30]] = 50.0          # a three-way tie at the top
+    logits[2, :] = 1.0                      # every logit equal
+    logits[3, 5] = -np.inf
+    logits[4, 7] = np.nan                   # never reported
+    for k in (1, 5, 40):
+        indices, values, probabilities = oracle_lib.top_k(logits, k)
+        for row in range(logits.shape[0]):
+            x = logits[row]
+            keep = np.flatnonzero(~np.isnan(x))
+            order = keep[np.lexsort((keep, -x[keep].astype(np.float64)))][:k]
+            np.testing.assert_array_equal(indices[row], order)
+            np.testing.assert_array_equal(values[row], x[order])
+            top = np.nanmax(x).astype(np.float64)
+            total = np.exp(x[keep].astype(np.float64) - top).sum()
+            if row != 4:  # the reference's sum runs over every logit; a NaN poisons it
+                np.testing.assert_allclose(probabilities[row],
+                                           np.exp(x[order].astype(np.float64) - top) / total,
+                                           rtol=1e-12)
+    indices, _, _ = oracle_lib.top_k(logits, 3)
+    assert list(indices[1]) == [10, 20, 30]
+    assert list(indices[2]) == [0, 1, 2]
+
+
 def test_attention_matches_float64_definition(oracle_lib):
     rng = np.random.default_rng(9)
     tokens, embed, heads = 17, 32, 4
