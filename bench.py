@@ -1,6 +1,6 @@
 #!/usr/bin/env python
-"""ViT forward-pass throughput on B200, one process per GPU (BASELINE config 4 by default:
-ViT-B/16, BF16, batch 256 per GPU, logits gathered to rank 0).
+"""ViT forward-pass throughput on B200, one process per GPU (by default the headline
+benchmark configuration: ViT-B/16, BF16, batch 256 per GPU, logits gathered to rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
                     [--config vit-b|vit-s|vit-ti|vit-l]

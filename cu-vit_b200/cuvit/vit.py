@@ -91,8 +91,9 @@ def tensor_specs(config: VitConfig) -> list[tuple[str, tuple[int, ...]]]:
 
 
 def random_weights(config: VitConfig, seed: int, std: float = 0.02) -> dict[str, np.ndarray]:
-    """Random-init weights as BASELINE's configs specify: matrices, class token and position
-    embedding ~ truncated normal (std, cut at +-2 std), LN gamma = 1, beta = 0, biases 0."""
+    """Random-init weights as the benchmark configurations specify: matrices, class token and
+    position embedding ~ truncated normal (std, cut at +-2 std), LN gamma = 1, beta = 0,
+    biases 0."""
     rng = np.random.default_rng(seed)
     weights = {}
     for name, extents in tensor_specs(config):

@@ -56,7 +56,8 @@ GEMM_CASES = [
     ("just over a tile", 65, 65, 65, False, 1.0, True, "none", "normal", 14),
     ("negative scale", 32, 48, 16, False, -2.5, True, "none", "normal", 15),
     ("scaled attention logits", 197, 197, 64, True, 0.125, False, "none", "normal", 16),
-    # ViT-Tiny QKV shape, U(-1, 1) from seed 0, then GELU and accumulate.
+    # The single-GEMM benchmark case: ViT-Tiny QKV shape, U(-1, 1) from seed 0, then GELU and
+    # accumulate.
     ("config1 qkv", 197, 576, 192, True, 1.0, True, "none", "uniform", 0),
     ("config1 gelu", 197, 768, 192, True, 1.0, True, "gelu", "uniform", 0),
     ("config1 accumulate", 197, 192, 768, True, 1.0, True, "accumulate", "uniform", 0),
@@ -105,7 +106,8 @@ def gelu_inputs():
 
 
 # Model cases: the reference vit_test's small config (tests/vit_test.cu:36-47), a head_dim-64
-# config that exercises the fused attention path, and ViT-Tiny/16 itself.
+# config that exercises the fused attention path, and ViT-Tiny/16 itself (the TF32 benchmark
+# configuration).
 VIT_CASES = [
     ("vit small", VitConfig(32, 8, 3, 24, 3, 4, 48, 7), 1234, 0.2, 3, 1),
     ("vit hd64", VitConfig(32, 8, 3, 128, 2, 2, 256, 10), 77, 0.05, 3, 2),

@@ -3,7 +3,7 @@
 Follows the reference's tests/gemm_test.cu case for case at its tolerances for FP32
 (term-scaled 1e-6: the FP32-faithful 3xTF32 tensor-core path and the FFMA path must both
 hold it), then the TF32 and BF16 modes at their own bounds, tile and pipeline edges, and
-BASELINE config 1 against the golden vectors from the reference's code.
+the single-GEMM benchmark case against the golden vectors from the reference's code.
 """
 
 from __future__ import annotations
@@ -328,7 +328,8 @@ def test_output_paths(math, c_dtype, n, ldc, accumulate, cuda):
 @pytest.mark.parametrize("label", ["config1 qkv", "config1 gelu", "config1 accumulate"])
 @pytest.mark.parametrize("math", [kernels.MATH_FP32, kernels.MATH_TF32], ids=["fp32", "tf32"])
 def test_baseline_config1_against_reference_golden(label, math, golden, cuda):
-    """BASELINE config 1 (ViT-Tiny QKV shape, U(-1,1) seed 0; GELU N=768; accumulate K=768)
+    """The single-GEMM benchmark case (ViT-Tiny QKV shape, U(-1,1) seed 0; GELU N=768;
+    accumulate K=768)
     against the outputs of the reference's own CPU code."""
     import make_golden as mg
 

@@ -1,11 +1,12 @@
 """The model runner on the GPU: logits against the reference's own CPU code (golden vectors)
 and the oracle, the properties tests/vit_test.cu pins (determinism, batch invariance,
-partial batches, limits, memory), and the BASELINE configurations at full size.
+partial batches, limits, memory), and the benchmark configurations (ViT-Ti/16 TF32 batch 32,
+ViT-S/16 and ViT-B/16 BF16 at batch 128 and 256, ViT-L/16 BF16) at full size.
 
 Tolerances (max-abs on logits unless noted):
   FP32 path   rtol 1e-4 + atol 1e-4, the reference's own (tests/vit_test.cu:125-130)
-  TF32 path   1e-3 max-abs
-  BF16 path   3e-2 max-abs and identical top-1
+  TF32 path   1e-3 max-abs (the parity bar for the TF32 mode)
+  BF16 path   3e-2 max-abs and identical top-1 (the parity bar for the BF16 mode)
 """
 
 from __future__ import annotations
@@ -235,7 +236,7 @@ def test_weight_file_path_matches_host_path(cuda):
 
 @pytest.mark.skipif(not oracle.ref_gpu_available(), reason="oracle/_ref GPU library not built")
 def test_tf32_path_against_reference_fp32_gpu_path(cuda):
-    """the TF32 path within 1e-3 of the reference's own FP32 GPU path
+    """The TF32 parity bar: the TF32 path within 1e-3 of the reference's own FP32 GPU path
     (src/model/vit.cu built for sm_100a, oracle/_ref), ViT-Tiny/16, 4 images."""
     import ctypes
 
@@ -268,7 +269,7 @@ def test_tf32_path_against_reference_fp32_gpu_path(cuda):
     assert np.abs(reference - cpu).max() <= 1e-4
 
 
-# BASELINE configs 2-4 at full batch; the oracle checks a sample of images (first, second,
+# The benchmark configurations at full batch; the oracle checks a sample of images (first, second,
 # last two) -- which also proves batch indexing at the far end -- and every logit is finite.
 FULL = [
     ("vit-ti b32 tf32", VitConfig(), 32, PRECISION_TF32, 1, TF32_TOL),
@@ -299,7 +300,7 @@ def test_baseline_configs_full_batch(label, config, batch, precision, seed, tol,
 
 
 def test_vit_l_bf16_against_fp32_path(cuda):
-    """BASELINE config 5's model (ViT-L/16: E = 1024, 16 heads, depth 24, MLP 4096) at 16
+    """The largest benchmark model (ViT-L/16: E = 1024, 16 heads, depth 24, MLP 4096) at 16
     images per GPU: BF16 logits within 3e-2 of the FP32-faithful path (which the oracle pins
     at 1e-4 on the smaller configs), top-1 identical outside near-ties."""
     config = VitConfig(embed_dim=1024, depth=24, heads=16, mlp_hidden=4096)
