@@ -329,8 +329,7 @@ def test_output_paths(math, c_dtype, n, ldc, accumulate, cuda):
 @pytest.mark.parametrize("math", [kernels.MATH_FP32, kernels.MATH_TF32], ids=["fp32", "tf32"])
 def test_baseline_config1_against_reference_golden(label, math, golden, cuda):
     """The single-GEMM benchmark case (ViT-Tiny QKV shape, U(-1,1) seed 0; GELU N=768;
-    accumulate K=768)
-    against the outputs of the reference's own CPU code."""
+    accumulate K=768) against the outputs of the reference's own CPU code."""
     import make_golden as mg
 
     case = next(c for c in mg.GEMM_CASES if c[0] == label)
