@@ -106,6 +106,22 @@ def test_elementwise_validation_matches_reference():
         kernels.launch_gelu(FAKE, FAKE, 1 << 62)
 
 
+def test_top_k_report_validation():
+    """cuvit_logits_top_k (the CLI's report_top on device logits): empty batches are no-ops,
+    bad extents and null operands fail on the host."""
+    kernels.launch_logits_top_k(None, None, None, None, 0, 1000, 5)
+    with pytest.raises(InvalidArgument, match="1 <= k <= classes"):
+        kernels.launch_logits_top_k(FAKE, FAKE, FAKE, FAKE, 2, 10, 11)
+    with pytest.raises(InvalidArgument, match="1 <= k <= classes"):
+        kernels.launch_logits_top_k(FAKE, FAKE, FAKE, FAKE, 2, 10, 0)
+    with pytest.raises(InvalidArgument, match="1 <= k <= classes"):
+        kernels.launch_logits_top_k(FAKE, FAKE, FAKE, FAKE, -1, 10, 3)
+    with pytest.raises(InvalidArgument, match="cannot be null"):
+        kernels.launch_logits_top_k(FAKE, None, FAKE, FAKE, 2, 10, 3)
+    lib = _lib.library()
+    assert lib.cuvit_vit_host_image_bytes(None) == 0
+
+
 def test_attention_validation():
     kernels.launch_attention(None, None, kernels.DTYPE_BF16, 0, 197, 12, 64, 0.125)
     with pytest.raises(Unsupported, match="head_dim 64"):
