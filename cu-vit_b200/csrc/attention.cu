@@ -182,7 +182,7 @@ __global__ void __launch_bounds__(kThreads)
         if (!ok) {
             // Wait until every MMA issued so far has finished before the CTA tears down.
             dev::tc_commit(bar_drain);
-            dev::mbar_wait(bar_drain, 0, p.status);
+            dev::mbar_drain_wait(bar_drain, 0);
         }
     } else if (warp >= 2) {
         // ---------------- softmax and output ----------------
@@ -509,7 +509,7 @@ __global__ void __launch_bounds__(kPipeThreads, 1)
         }
         if (!ok) {
             dev::tc_commit(bar_drain);
-            dev::mbar_wait(bar_drain, 0, p.status);
+            dev::mbar_drain_wait(bar_drain, 0);
         }
     } else if (warp >= 4) {
         // ---------------- softmax and output ----------------

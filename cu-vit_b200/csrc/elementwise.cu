@@ -493,16 +493,25 @@ __global__ void __launch_bounds__(kThreads)
         return;
     }
     const float* const x = logits + static_cast<long long>(row) * classes;
+    // NaN logits take no part: fmaxf drops them from the maximum, the sum skips them, and the
+    // picks below never select one (every comparison with NaN is false). The sum and the
+    // probabilities are double, as in report_top.
     float maximum = -INFINITY;
     for (int c = lane; c < classes; c += kWarp) {
         maximum = fmaxf(maximum, __ldg(x + c));
     }
     maximum = warp_max(maximum);
-    float total = 0.0F;
+    double total = 0.0;
     for (int c = lane; c < classes; c += kWarp) {
-        total += expf(__ldg(x + c) - maximum);
+        const float v = __ldg(x + c);
+        if (v == v) {
+            total += exp(static_cast<double>(v) - static_cast<double>(maximum));
+        }
     }
-    total = warp_sum(total);
+#pragma unroll
+    for (int offset = 16; offset > 0; offset /= 2) {
+        total += __shfl_xor_sync(0xFFFFFFFFu, total, offset);
+    }
     float last_value = INFINITY;
     int last_index = -1;
     const long long out = static_cast<long long>(row) * k;
@@ -533,7 +542,12 @@ __global__ void __launch_bounds__(kThreads)
         if (lane == 0) {
             indices[out + r] = best_index;
             values[out + r] = best_index < 0 ? NAN : best_value;
-            probabilities[out + r] = best_index < 0 ? 0.0F : expf(best_value - maximum) / total;
+            probabilities[out + r] =
+                best_index < 0
+                    ? 0.0F
+                    : static_cast<float>(exp(static_cast<double>(best_value) -
+                                             static_cast<double>(maximum)) /
+                                         total);
         }
         if (best_index >= 0) {
             last_value = best_value;

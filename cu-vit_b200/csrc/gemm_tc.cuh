@@ -512,7 +512,7 @@ __global__ void __launch_bounds__(TcShape<ElemBytes, BN, Split>::kThreads, 1)
             // Drain: the commit arrives once every MMA issued so far has completed, so no
             // MMA still reads shared memory or writes TMEM when the CTA tears down.
             dev::tc_commit(drain_bar);
-            dev::mbar_wait(drain_bar, 0, p.status);
+            dev::mbar_drain_wait(drain_bar, 0);
         }
     } else if (warp >= 4 && warp < 4 + kEpilogueWarps) {
         // ---------------- epilogue ----------------

@@ -227,7 +227,7 @@ __global__ void __launch_bounds__(PairShape<BN>::kThreads, 1)
         // Every MMA issued has completed (so none still reads either CTA's shared memory or
         // writes TMEM) before this thread reaches the closing cluster barrier.
         dev::tc_commit_pair(dev::map_to_rank(drain_bar, 0));
-        dev::mbar_wait(drain_bar, 0, p.status);
+        dev::mbar_drain_wait(drain_bar, 0);
     } else if (warp >= 4 && warp < 4 + kEpilogueWarps) {
         // ---------------- epilogue (both CTAs, this CTA's 128 rows) ----------------
         const int e = warp - 4;

@@ -95,6 +95,19 @@ int current_context(const DeviceContext** context) {
 
 bool is_blackwell(const DeviceContext& context) { return context.major == 10; }
 
+int peek_device_status() {
+    const DeviceContext* context = nullptr;
+    CUVIT_TRY(current_context(&context));
+    unsigned value = 0;
+    CUVIT_TRY_CUDA(cudaMemcpy(&value, context->status, sizeof(value), cudaMemcpyDeviceToHost));
+    if (value & cuvit::dev::kStatusTimeout) {
+        return fail(CUVIT_DEVICE_TIMEOUT,
+                    "a kernel gave up on a bounded device-side wait; outputs are undefined "
+                    "(cuvit_device_status() clears the flag)");
+    }
+    return CUVIT_OK;
+}
+
 namespace {
 thread_local bool t_reverse_sweep = false;
 } // namespace

@@ -94,6 +94,10 @@ struct DeviceContext {
 // Context of the current device, initialised on first use (thread-safe).
 int current_context(const DeviceContext** context);
 
+// Reads the current device's status word without clearing it (after the caller has
+// synchronized the work it wants covered). CUVIT_DEVICE_TIMEOUT when a bounded wait gave up.
+int peek_device_status();
+
 // True for sm_100 parts, where the tcgen05 kernels can run.
 bool is_blackwell(const DeviceContext& context);
 

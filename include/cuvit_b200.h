@@ -211,9 +211,10 @@ int cuvit_round_to_tf32(const float* input, float* output, int64_t count,
  * on the host): for each of `batch` rows of `classes` device logits, the k largest in
  * descending order -- equal logits by ascending class index, where the reference's
  * partial_sort leaves their order open -- into device arrays [batch, k]: class indices,
- * logits, and softmax probabilities exp(logit - max) / sum_j exp(logit_j - max). NaN logits
- * are never reported; a row with fewer than k others reports index -1, value NaN and
- * probability 0 in the remaining places. 1 <= k <= classes. */
+ * logits, and softmax probabilities exp(logit - max) / sum_j exp(logit_j - max), summed and
+ * divided in double like the reference. NaN logits take no part: they are left out of the
+ * maximum and the sum and are never reported; a row with fewer than k other logits reports
+ * index -1, value NaN and probability 0 in the remaining places. 1 <= k <= classes. */
 int cuvit_logits_top_k(const float* logits, int batch, int classes, int k, int* indices,
                        float* values, float* probabilities, cuvit_stream_t stream);
 
@@ -233,7 +234,14 @@ int cuvit_attention(const void* qkv, void* context, int dtype, int batch, int to
 
 /* Reads and clears the device status word of the current device, after synchronizing it.
  * *flags receives the bits set since the last call (0 = clean). Returns
- * CUVIT_DEVICE_TIMEOUT when a kernel gave up on a bounded wait. */
+ * CUVIT_DEVICE_TIMEOUT when a kernel gave up on a bounded wait.
+ * The word is one per device and per process: every model, stream and host thread of the
+ * process that launches on that device shares it. Once a kernel has timed out, every later
+ * wait on that device that does not complete within its first few spins also gives up (so
+ * a stuck device drains quickly instead of each kernel waiting out the full limit), until
+ * some caller reads the word here; that read clears it for every user of the device. Callers
+ * that share a device should therefore agree on who checks it. cuvit_vit_forward_host()
+ * checks it (without clearing) after its pass and returns CUVIT_DEVICE_TIMEOUT when set. */
 int cuvit_device_status(unsigned* flags);
 
 /* Diagnostic: launches one thread that waits on a barrier nothing will release, with a
@@ -295,7 +303,9 @@ int cuvit_vit_forward(cuvit_vit* model, const float* images, float* logits, int 
  * creation, so it allocates nothing per call. Batches of 64 images and more run in two
  * halves: the second half's copy runs on a second stream while the first half computes,
  * which needs pinned host memory to overlap. Logits do not depend on the chunking (every
- * image's result is independent of the batch it runs in). */
+ * image's result is independent of the batch it runs in). Returns CUVIT_DEVICE_TIMEOUT,
+ * with undefined logits, when the device status word is set after the pass (it is left set;
+ * see cuvit_device_status). */
 int cuvit_vit_forward_host(cuvit_vit* model, const float* images, float* logits, int batch,
                            cuvit_stream_t stream);
 /* forward_host() without the final synchronisation, for serving loops: queues the copy of

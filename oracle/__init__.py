@@ -29,10 +29,12 @@ _i64 = ctypes.c_int64
 _f = ctypes.c_float
 
 
-def build(reference: bool = False) -> None:
-    """Builds liboracle.so (and the _ref libraries when reference=True)."""
+def build(reference: bool = False, source=None) -> None:
+    """Builds liboracle.so (and, when reference=True, the _ref libraries from the Cu-Vit
+    source checkout `source`; the Makefile's default is a checkout beside this repository)."""
     targets = ["oracle"] + (["ref", "ref-tests"] if reference else [])
-    subprocess.run(["make", "-s", "-C", str(HERE), *targets], check=True)
+    extra = [f"REF={source}"] if reference and source is not None else []
+    subprocess.run(["make", "-s", "-C", str(HERE), *extra, *targets], check=True)
 
 
 def _load(path: pathlib.Path, key: str) -> ctypes.CDLL:
@@ -242,3 +244,47 @@ def ref_gpu() -> ctypes.CDLL:
     library.ref_gpu_vit_forward.restype = _i
     library.ref_gpu_vit_destroy.argtypes = [ctypes.c_void_p]
     return library
+
+
+class RefGpuModel:
+    """The reference's own VisionTransformer (FP32 GPU path, oracle/_ref/libcuvit_ref_gpu.so)
+    for `config` and host `weights`, loaded through a temporary .cvw file. forward() takes
+    device pointers (integers) and runs on `stream` (a cudaStream_t as an integer, 0 for the
+    legacy default stream)."""
+
+    def __init__(self, config, weights: dict, specs, max_batch: int):
+        import tempfile
+
+        from cuvit import cvw
+
+        self.config = config
+        with tempfile.TemporaryDirectory() as tmp:
+            path = pathlib.Path(tmp) / "weights.cvw"
+            writer = cvw.WeightFileWriter()
+            for name, extents in specs:
+                writer.add(name, extents, weights[name])
+            writer.write(path)
+            ints = config_ints(config)
+            self._handle = ref_gpu().ref_gpu_vit_create(str(path).encode(), ints.ctypes.data,
+                                                        config.layer_norm_epsilon, max_batch)
+        if not self._handle:
+            raise RuntimeError("the reference's VisionTransformer could not be created")
+
+    def forward(self, images_ptr: int, logits_ptr: int, batch: int, stream: int = 0) -> None:
+        status = ref_gpu().ref_gpu_vit_forward(self._handle, ctypes.c_void_p(images_ptr),
+                                               ctypes.c_void_p(logits_ptr), batch,
+                                               ctypes.c_void_p(stream or None))
+        if status != 0:
+            raise RuntimeError("the reference's GPU forward pass failed")
+
+    def close(self) -> None:
+        if self._handle:
+            ref_gpu().ref_gpu_vit_destroy(self._handle)
+            self._handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:  # interpreter shutdown
+            pass
+

@@ -152,13 +152,17 @@ void oracle_top_k(const float* logits, int batch, int classes, int k, int* indic
                   float* values, double* probabilities) {
     for (int row = 0; row < batch; ++row) {
         const float* const x = logits + (int64_t)row * classes;
-        float maximum = x[0];
-        for (int c = 1; c < classes; ++c) {
+        /* NaN logits take no part in the maximum, the sum or the picks (the reference's
+         * partial_sort leaves a row with NaNs unordered, so the rule is this library's). */
+        float maximum = -INFINITY;
+        for (int c = 0; c < classes; ++c) {
             maximum = x[c] > maximum ? x[c] : maximum;
         }
         double total = 0.0;
         for (int c = 0; c < classes; ++c) {
-            total += exp((double)x[c] - maximum);
+            if (x[c] == x[c]) {
+                total += exp((double)x[c] - maximum);
+            }
         }
         float last_value = INFINITY;
         int last_index = -1;

@@ -225,6 +225,34 @@ def test_logits_top_k_matches_the_report(batch, classes, k, cuda):
                                     classes, classes + 1)
 
 
+def test_logits_top_k_skips_nan(cuda):
+    """NaN logits take no part in the report: not in the maximum (a NaN in column 0 used to
+    seed it), not in the sum of exponentials, never picked; a row with fewer than k finite
+    logits pads with index -1, value NaN, probability 0."""
+    rng = np.random.default_rng(5)
+    batch, classes, k = 4, 50, 5
+    logits = rng.standard_normal((batch, classes)).astype(np.float32)
+    logits[0, 0] = np.nan
+    logits[1, 25] = np.nan
+    logits[1, 26] = logits[1].max() + 2.0 if np.isfinite(logits[1]).all() else 10.0
+    logits[2, :] = np.nan
+    logits[2, 7] = 1.5
+    logits[2, 9] = -0.5
+    logits[3, ::2] = np.nan
+    want_i, want_v, want_p = oracle.top_k(logits, k)
+    assert want_i[2, 2] == -1 and want_p[2, 2] == 0.0
+    assert np.isfinite(want_p).all() and np.isfinite(want_v[0]).all()
+    indices = cuda.zeros((batch, k), dtype=cuda.int32, device="cuda")
+    values = cuda.zeros((batch, k), device="cuda")
+    probabilities = cuda.zeros((batch, k), device="cuda")
+    kernels.launch_logits_top_k(to_device(logits), indices, values, probabilities, batch,
+                                classes, k)
+    cuda.cuda.synchronize()
+    np.testing.assert_array_equal(indices.cpu().numpy(), want_i)
+    np.testing.assert_array_equal(values.cpu().numpy(), want_v)
+    np.testing.assert_allclose(probabilities.cpu().numpy(), want_p, rtol=1e-6, atol=1e-30)
+
+
 def test_invalid_arguments_on_device_buffers(cuda):
     buffer = to_device(np.zeros(16))
     kernels.launch_gelu(buffer, buffer, 0)
