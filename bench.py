@@ -67,6 +67,8 @@ def parse_args():
     parser.add_argument("--config", choices=sorted(CONFIGS), default="vit-b")
     parser.add_argument("--profile-passes", type=int, default=5)
     parser.add_argument("--no-cpu-baseline", action="store_true")
+    parser.add_argument("--no-extras", action="store_true",
+                        help="skip the other configurations, single GEMMs and FP32 baselines")
     return parser.parse_args()
 
 
@@ -150,6 +152,17 @@ def write_cvw(config, weights, path) -> None:
     writer.write(path)
 
 
+def cpu_model() -> str:
+    """The host CPU's model name (from /proc/cpuinfo), for the CPU baseline's record."""
+    try:
+        for line in pathlib.Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
 def cpu_reference_step(config, weights_path, images, threads):
     """One bounded sample of the workload through the reference's CPU code: returns
     (seconds, images, kind)."""
@@ -200,6 +213,7 @@ def reference_arm(args) -> None:
         "config": {"workload": f"{label} forward, reference CPU implementation (FP32)",
                    "model": label, "seq_len": config.token_count()},
         "cpu_baseline": {"value": value, "unit": "images/s", "cores": threads, "kind": kind,
+                         "cpu": cpu_model(),
                          "sample": f"{count} images in {rounds} rounds of {threads}, one per "
                                    "host thread, VitReference::forward "
                                    "(tests/reference/vit.hpp)"},
@@ -207,6 +221,197 @@ def reference_arm(args) -> None:
                 "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
+
+
+def profile_pass_kinds(model, images, logits, batch, stream, passes: int) -> dict:
+    """Per launch kind, the median over `passes` profiled passes (CUDA events around every
+    launch, after one discarded pass) of launches, ms, FLOPs and bytes per pass."""
+    model.forward_profiled(images, logits, batch, stream)
+    per_pass: list[dict[str, dict]] = []
+    for _ in range(max(passes, 1)):
+        kinds: dict[str, dict] = {}
+        for r in model.forward_profiled(images, logits, batch, stream):
+            entry = kinds.setdefault(r["kind"], {"launches": 0, "ms": 0.0, "flops": 0.0,
+                                                 "bytes": 0.0})
+            entry["launches"] += 1
+            entry["ms"] += r["ms"]
+            entry["flops"] += r["flops"]
+            entry["bytes"] += r["bytes"]
+        per_pass.append(kinds)
+    by_kind = {}
+    for kind in per_pass[0]:
+        times = sorted(k[kind]["ms"] for k in per_pass)
+        by_kind[kind] = dict(per_pass[0][kind], ms=times[len(times) // 2])
+    return by_kind
+
+
+def gemm_summary(by_kind: dict) -> tuple[float, float, int]:
+    """(GEMM FLOPs, GEMM ms, GEMM launches) of one pass."""
+    gemm = [e for k, e in by_kind.items() if k.startswith("gemm")]
+    return (sum(e["flops"] for e in gemm), sum(e["ms"] for e in gemm),
+            sum(e["launches"] for e in gemm))
+
+
+def event_ms(torch, stream, fn, repeats: int) -> float:
+    """Mean device milliseconds of fn() over `repeats` back-to-back calls on `stream`."""
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for _ in range(repeats):
+        fn()
+    end.record(stream)
+    end.synchronize()
+    return start.elapsed_time(end) / repeats
+
+
+def measure_tf32_peak(torch, device) -> float:
+    """Dense TF32 tensor-core throughput of torch.matmul (cuBLAS) at 8192^3, best of 10,
+    CUDA events: the denominator of the TF32 configuration's roofline."""
+    previous = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = True
+    a = torch.randn(8192, 8192, device=device)
+    b = torch.randn(8192, 8192, device=device)
+    stream = torch.cuda.current_stream(device)
+    torch.matmul(a, b)
+    best = min(event_ms(torch, stream, lambda: torch.matmul(a, b), 1) for _ in range(10))
+    torch.backends.cuda.matmul.allow_tf32 = previous
+    del a, b
+    return 2 * 8192 ** 3 / (best * 1e-3) / 1e12
+
+
+def measure_other_configs(torch, device, peak_bf16: float, peak_tf32: float) -> dict:
+    """The benchmark configurations other than the headline one, each on one GPU with its own
+    model: images/s over 20 graph replays (inputs resident), GEMM TFLOP/s from 3 profiled
+    passes, and that as a fraction of the measured tensor peak of its precision."""
+    import cuvit
+    from cuvit.vit import PRECISION_BF16, PRECISION_TF32, VisionTransformer, VitConfig, random_weights
+
+    results = {}
+    stream = torch.cuda.current_stream(device)
+    for name in ("vit-ti", "vit-s", "vit-l"):
+        label, kwargs, batch, precision_name, seed = CONFIGS[name]
+        config = VitConfig(**kwargs)
+        precision = PRECISION_BF16 if precision_name == "bf16" else PRECISION_TF32
+        model = VisionTransformer(config, random_weights(config, seed), max_batch=batch,
+                                  precision=precision, device=device.index)
+        rng = np.random.default_rng([seed, 0])
+        images = torch.from_numpy(rng.standard_normal(batch * config.image_elements())
+                                  .astype(np.float32)).to(device)
+        logits = torch.zeros(batch, config.classes, device=device)
+        for _ in range(5):
+            model.forward_graph(images, logits, batch, stream)
+        ms = event_ms(torch, stream, lambda: model.forward_graph(images, logits, batch, stream),
+                      20)
+        flops, gemm_ms, _ = gemm_summary(profile_pass_kinds(model, images, logits, batch,
+                                                            stream, 3))
+        cuvit.kernels.device_status()  # raises if any kernel gave up on a bounded wait
+        peak = peak_bf16 if precision == PRECISION_BF16 else peak_tf32
+        tflops = flops / (gemm_ms * 1e-3) / 1e12
+        results[name] = {
+            "workload": f"{label} {precision_name.upper()}, batch {batch}", "batch": batch,
+            "images_per_s": batch / (ms * 1e-3), "ms_per_pass": ms,
+            "gemm_tflops": tflops, "gemm_frac": tflops / peak,
+            "peak": peak, "peak_kind": ("measured bf16 burst (MEASURED_PEAKS.json)"
+                                        if precision == PRECISION_BF16 else
+                                        "measured tf32 burst (torch.matmul 8192^3, this run)"),
+            "pass_tflops": batch * config.gflop_per_image() / ms,
+        }
+        model.close()
+        del images, logits
+    return results
+
+
+def measure_single_gemms(torch, device, peak_tf32: float) -> dict:
+    """the three single FP32 GEMMs of ViT-Tiny (QKV shape without
+    epilogue, FC1 shape with GELU, FC2 shape accumulating), A, B, bias ~ U(-1, 1) from seed 0,
+    through launch_gemm in the FP32-faithful (3xTF32) and TF32 modes. Mean device time per
+    launch over 100 launches captured in one CUDA graph (so host call overhead does not
+    appear), 5 replays; each launch is one wave or less, so this is a latency figure."""
+    from cuvit import kernels
+
+    stream = torch.cuda.current_stream(device)
+    rng = np.random.default_rng(0)
+    shapes = [("qkv", 197, 576, 192, False, False), ("fc1_gelu", 197, 768, 192, True, False),
+              ("fc2_accumulate", 197, 192, 768, False, True)]
+    results = {}
+    previous = kernels.get_math_mode()
+    for math_name, math in (("fp32", kernels.MATH_FP32), ("tf32", kernels.MATH_TF32)):
+        kernels.set_math_mode(math)
+        for name, m, n, k, gelu, accumulate in shapes:
+            a = torch.from_numpy(rng.uniform(-1, 1, m * k).astype(np.float32)).to(device)
+            b = torch.from_numpy(rng.uniform(-1, 1, n * k).astype(np.float32)).to(device)
+            bias = torch.from_numpy(rng.uniform(-1, 1, n).astype(np.float32)).to(device)
+            c = torch.zeros(m * n, device=device)
+            problem = kernels.gemm_problem(m, n, k, kernels.LAYOUT_TRANSPOSED)
+            problem.epilogue.gelu = int(gelu)
+            problem.epilogue.accumulate = int(accumulate)
+
+            side = torch.cuda.Stream(device)
+            side.wait_stream(stream)
+            with torch.cuda.stream(side):
+                for _ in range(3):  # one-time set-up happens outside the capture
+                    kernels.launch_gemm(a, b, bias, c, problem, side)
+            stream.wait_stream(side)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=side):
+                for _ in range(100):
+                    kernels.launch_gemm(a, b, bias, c, problem, side)
+            graph.replay()
+            ms = event_ms(torch, stream, graph.replay, 5) / 100
+            del graph
+            flops = 2.0 * m * n * k
+            results[f"{name}_{math_name}"] = {
+                "m": m, "n": n, "k": k, "us_per_launch": ms * 1e3,
+                "tflops": flops / (ms * 1e-3) / 1e12,
+                "frac_of_tf32_peak": flops / (ms * 1e-3) / 1e12 / peak_tf32}
+    kernels.set_math_mode(previous)
+    kernels.device_status()
+    return results
+
+
+def measure_fp32_baselines(torch, device) -> dict:
+    """ViT-B/16 at batch 256 in FP32 on one GPU: the reference's own FP32 GPU path
+    (src/model/vit.cu built for sm_100a into oracle/_ref; a second baseline, never the
+    product) beside this library's FP32-faithful mode (3xTF32 tensor cores, the reference's
+    unfused attention steps)."""
+    import oracle
+    import cuvit
+    from cuvit.vit import PRECISION_FP32, VisionTransformer, VitConfig, random_weights, tensor_specs
+
+    label, kwargs, batch, _, seed = CONFIGS["vit-b"]
+    config = VitConfig(**kwargs)
+    weights = random_weights(config, seed)
+    stream = torch.cuda.current_stream(device)
+    rng = np.random.default_rng([seed, 0])
+    images = torch.from_numpy(rng.standard_normal(batch * config.image_elements())
+                              .astype(np.float32)).to(device)
+    logits = torch.zeros(batch, config.classes, device=device)
+    results = {"workload": f"{label} FP32, batch {batch}"}
+    ours = VisionTransformer(config, weights, max_batch=batch, precision=PRECISION_FP32,
+                             device=device.index)
+    for _ in range(2):
+        ours.forward_graph(images, logits, batch, stream)
+    ms = event_ms(torch, stream, lambda: ours.forward_graph(images, logits, batch, stream), 3)
+    cuvit.kernels.device_status()
+    ours.close()
+    results["ours_fp32_faithful"] = {"images_per_s": batch / (ms * 1e-3), "ms_per_pass": ms}
+    if oracle.ref_gpu_available():
+        ref = oracle.RefGpuModel(config, weights, tensor_specs(config), batch)
+        handle = stream.cuda_stream
+
+        def ref_pass():
+            ref.forward(images.data_ptr(), logits.data_ptr(), batch, handle)
+
+        ref_pass()
+        ms_ref = event_ms(torch, stream, ref_pass, 3)
+        ref.close()
+        results["reference_fp32_gpu"] = {"images_per_s": batch / (ms_ref * 1e-3),
+                                         "ms_per_pass": ms_ref,
+                                         "kind": "reference (oracle/_ref/libcuvit_ref_gpu.so)"}
+        results["ratio_ours_over_reference"] = ms_ref / ms
+    else:
+        results["reference_fp32_gpu"] = None
+    return results
 
 
 def our_arm(args) -> None:
@@ -279,25 +484,12 @@ def our_arm(args) -> None:
     gpu_launches = model.launches_per_forward(batch) * args.steps
     launches_issued = cuvit.kernels.launch_count() - launches_before  # 0 under graph replay
 
+    cuvit.kernels.device_status()  # raises if any kernel of the timed passes gave up a wait
+
     # Per-kernel device time over profiled passes (events around each launch), after one
     # discarded pass; per launch kind, the median pass (clocks drift under the power cap).
-    model.forward_profiled(images, logits, batch, stream)
-    per_pass: list[dict[str, dict]] = []
-    for _ in range(max(args.profile_passes, 1)):
-        kinds: dict[str, dict] = {}
-        for r in model.forward_profiled(images, logits, batch, stream):
-            entry = kinds.setdefault(r["kind"], {"launches": 0, "ms": 0.0, "flops": 0.0,
-                                                 "bytes": 0.0})
-            entry["launches"] += 1
-            entry["ms"] += r["ms"]
-            entry["flops"] += r["flops"]
-            entry["bytes"] += r["bytes"]
-        per_pass.append(kinds)
-    passes = 1  # by_kind below holds one (median) pass
-    by_kind = {}
-    for kind in per_pass[0]:
-        times = sorted(k[kind]["ms"] for k in per_pass)
-        by_kind[kind] = dict(per_pass[0][kind], ms=times[len(times) // 2])
+    by_kind = profile_pass_kinds(model, images, logits, batch, stream, args.profile_passes)
+    passes = 1  # by_kind holds one (median) pass
     profiled_ms = sum(e["ms"] for e in by_kind.values())
     kernels = {}
     for kind, e in sorted(by_kind.items()):
@@ -308,10 +500,8 @@ def our_arm(args) -> None:
             "tflops": e["flops"] / (e["ms"] * 1e-3) / 1e12 if e["flops"] else None,
             "gbs": e["bytes"] / (e["ms"] * 1e-3) / 1e9,
         }
-    gemm = [e for k, e in by_kind.items() if k.startswith("gemm")]
-    gemm_flops = sum(e["flops"] for e in gemm)
-    gemm_ms = sum(e["ms"] for e in gemm)
-    gemm_launches = sum(e["launches"] for e in gemm)
+    gemm_flops, gemm_ms, gemm_launches = gemm_summary(by_kind)
+    cuvit.kernels.device_status()
     achieved_tflops = gemm_flops / (gemm_ms * 1e-3) / 1e12
     peak, peak_kind = peaks()
     traffic, traffic_launch = gemm_traffic(args.config, label, batch, precision_name)
@@ -354,10 +544,23 @@ def our_arm(args) -> None:
     e2e_end.record(stream)
     barrier()
     e2e_ms = max_over_ranks(e2e_start.elapsed_time(e2e_end))
+    cuvit.kernels.device_status()
 
     cpu_baseline = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu_baseline = measure_cpu_baseline(config, weights, seed)
+
+    # One GPU only: the other benchmark configurations, the single-GEMM configuration and the
+    # FP32 comparison with the reference's own GPU path, each timed in this run beside the
+    # headline (which they do not touch).
+    extras = {}
+    if world == 1 and not args.no_extras:
+        peak_tf32 = measure_tf32_peak(torch, device)
+        extras["tf32_peak_tflops"] = peak_tf32
+        extras["configs"] = measure_other_configs(
+            torch, device, peak.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]), peak_tf32)
+        extras["single_gemms"] = measure_single_gemms(torch, device, peak_tf32)
+        extras["fp32_baselines"] = measure_fp32_baselines(torch, device)
 
     total_images = world * batch * args.steps
     value = total_images / (elapsed_ms * 1e-3)
@@ -388,9 +591,10 @@ def our_arm(args) -> None:
                 "kernel": "tcgen05 GEMMs, all launches of a pass (tc_gemm_pair_kernel: patch, "
                           "QKV, proj, FC2; tc_gemm_kernel: FC1 with GELU, head)",
                 "bound": "tensor", "achieved": achieved_tflops,
-                "peak": sustained, "unit": "TFLOP/s", "frac": achieved_tflops / sustained,
-                "peak_kind": f"{peak_kind} bf16 sustained (GEMMs run inside a long step)",
-                "frac_of_burst": achieved_tflops / burst,
+                "peak": burst, "unit": "TFLOP/s", "frac": achieved_tflops / burst,
+                "peak_kind": f"{peak_kind} bf16 burst (each GEMM timed per launch with CUDA "
+                             "events inside ~11 ms profiled passes)",
+                "frac_of_sustained": achieved_tflops / sustained,
                 "frac_of_nominal_2250": achieved_tflops / 2250.0,
                 "traffic": traffic,
                 "traffic_launch": traffic_launch,
@@ -401,6 +605,7 @@ def our_arm(args) -> None:
             "clocks": clocks,
             "cpu_baseline": cpu_baseline,
             "launches_issued_in_timed_region": launches_issued,
+            **extras,
         }
         print(json.dumps(line), flush=True)
     model.close()
@@ -440,6 +645,7 @@ def measure_cpu_baseline(config, weights, seed) -> dict | None:
         return {"value": None, "unit": "images/s", "cores": threads, "kind": None,
                 "sample": f"unavailable: {error}"}
     return {"value": count / seconds, "unit": "images/s", "cores": threads, "kind": kind,
+            "cpu": cpu_model(),
             "sample": f"{count} images, one per host thread, VitReference::forward "
                       f"(tests/reference/vit.hpp), {seconds:.1f} s"}
 

@@ -74,7 +74,7 @@ std::vector<TensorSpec> tensor_specs(const cuvit_vit_config& c) {
     }
     specs.push_back({"norm.weight", {e}, false});
     specs.push_back({"norm.bias", {e}, false});
-    // The head stays FP32 in every precision (see run_forward).
+    // The head's weights stay in float storage in every precision (see run_forward).
     specs.push_back({"head.weight", {c.classes, e}, false});
     specs.push_back({"head.bias", {c.classes}, false});
     return specs;
@@ -550,19 +550,23 @@ int run_forward(cuvit_vit& m, const void* images, float* logits, int batch, cuda
     }
 
     // Only the class token feeds the head (src/model/vit.cu:309-316), so only those rows
-    // are normalised. The final norm's output, the head's weights and its GEMM stay
-    // FP32-faithful (3xTF32) in every precision: a BF16 head added ~1e-3 RMS of error straight
-    // onto the logits, for 0.4 GFLOP of the 9 TFLOP of a ViT-B/16 pass at batch 256.
+    // are normalised. The final norm's output and the head's weights stay in float storage
+    // and the head runs with TF32 operands rounded to nearest (FP32-faithful in the FP32
+    // model): in a BF16 head the bfloat16 roundings of those two added 1.2e-3 RMS straight
+    // onto the ViT-B/16 logits, a third of the BF16 path's whole logit error, where the TF32
+    // head adds an eighth of that for 0.4 of the 9 TFLOP of a pass at batch 256.
+    const int head_math = m.precision == CUVIT_MATH_FP32 ? CUVIT_MATH_FP32 : CUVIT_MATH_TF32;
+    const int head_dtype = m.precision == CUVIT_MATH_FP32 ? CUVIT_DTYPE_F32 : CUVIT_DTYPE_TF32;
     CUVIT_LAUNCH(CUVIT_KIND_LAYER_NORM, -1, 0.0, b * e * 8.0 + 8.0 * e,
                  cuvit_layer_norm_ex(m.tokens, static_cast<int64_t>(tokens) * e, m.final_gamma,
-                                     m.final_beta, m.class_rows, CUVIT_DTYPE_F32, e, batch, e,
+                                     m.final_beta, m.class_rows, head_dtype, e, batch, e,
                                      c.layer_norm_epsilon, s));
     cuvit_gemm_problem head;
     cuvit_gemm_problem_init(&head, batch, c.classes, e, CUVIT_LAYOUT_TRANSPOSED);
     CUVIT_LAUNCH(CUVIT_KIND_GEMM_HEAD, -1, 2.0 * b * c.classes * e,
                  b * e * 4.0 + double(c.classes) * e * 4.0 + 4.0 * c.classes + 4.0 * b * c.classes,
                  cuvit_gemm_ex(m.class_rows, m.head_weight, m.head_bias, logits, CUVIT_DTYPE_F32,
-                               CUVIT_MATH_FP32, &head, s));
+                               head_math, &head, s));
     return CUVIT_OK;
 }
 
@@ -627,7 +631,10 @@ int build(cuvit_vit* m, const float* const* host) {
             status = host::check_cuda(
                 cudaMemcpy(target, host[i], count * sizeof(float), cudaMemcpyHostToDevice),
                 "cudaMemcpy(weights)");
-            if (status == CUVIT_OK && spec.gemm_weight && m->precision == CUVIT_MATH_TF32) {
+            const bool tf32_operand =
+                (spec.gemm_weight && m->precision == CUVIT_MATH_TF32) ||
+                (spec.name == "head.weight" && m->precision != CUVIT_MATH_FP32);
+            if (status == CUVIT_OK && tf32_operand) {
                 // TF32 operands are rounded to nearest once here; the tensor core would
                 // otherwise truncate them on every use.
                 float* const values = static_cast<float*>(target);
