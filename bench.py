@@ -67,6 +67,8 @@ def parse_args():
     parser.add_argument("--config", choices=sorted(CONFIGS), default="vit-b")
     parser.add_argument("--profile-passes", type=int, default=5)
     parser.add_argument("--no-cpu-baseline", action="store_true")
+    parser.add_argument("--timeline", action="store_true",
+                        help="device timeline of one graph-replayed pass (instrumented build)")
     parser.add_argument("--no-extras", action="store_true",
                         help="skip the other configurations, single GEMMs and FP32 baselines")
     return parser.parse_args()
@@ -650,9 +652,109 @@ def measure_cpu_baseline(config, weights, seed) -> dict | None:
                       f"(tests/reference/vit.hpp), {seconds:.1f} s"}
 
 
+def timeline_arm(args) -> None:
+    """Where a graph-replayed pass spends its time between and inside kernels (one GPU).
+
+    Needs the instrumented library (python cu-vit_b200/build.py --timeline): every
+    forward-path kernel stamps the global timer at its first CTA's entry and its last warp's
+    exit, and CTA 0 its SM cycle counter, so each launch gives its span, the gap before it
+    and the SM clock it ran at. Three passes are replayed back to back as in the timed region
+    of the benchmark; the device is synchronized once after them and one more replay is
+    recorded (a graph node keeps its grid id across replays, so one replay is recorded at a
+    time); then one profiled pass (CUDA events around every launch) for comparison."""
+    import ctypes
+
+    import torch
+
+    import cuvit
+    from cuvit import _lib
+    from cuvit.errors import check
+    from cuvit.vit import PRECISION_BF16, PRECISION_TF32, VisionTransformer, VitConfig, random_weights
+
+    lib = _lib.library()
+    if not lib.cuvit_timeline_available():
+        raise SystemExit("the timeline build is not loaded (build it with "
+                         "python cu-vit_b200/build.py --timeline)")
+    label, kwargs, batch, precision_name, seed = CONFIGS[args.config]
+    config = VitConfig(**kwargs)
+    precision = PRECISION_BF16 if precision_name == "bf16" else PRECISION_TF32
+    device = torch.device("cuda", 0)
+    model = VisionTransformer(config, random_weights(config, seed), max_batch=batch,
+                              precision=precision)
+    rng = np.random.default_rng([seed, 0])
+    images = torch.from_numpy(rng.standard_normal(batch * config.image_elements())
+                              .astype(np.float32)).to(device)
+    logits = torch.zeros(batch, config.classes, device=device)
+    stream = torch.cuda.current_stream(device)
+    kinds = [r["kind"] for r in model.forward_profiled(images, logits, batch, stream)]
+    per_pass = len(kinds)
+
+    def capture(run, passes):
+        check(lib.cuvit_timeline_reset())
+        run()
+        torch.cuda.synchronize()
+        records = (_lib.TimelineRecordC * (per_pass * passes + 16))()
+        count = ctypes.c_int(0)
+        check(lib.cuvit_timeline_read(records, len(records), ctypes.byref(count)))
+        got = records[:count.value]
+        if len(got) != per_pass * passes:
+            raise SystemExit(f"expected {per_pass * passes} launches, recorded {len(got)}")
+        return got[-per_pass:]
+
+    def analyse(records):
+        rows = []
+        for i, (kind, r) in enumerate(zip(kinds, records)):
+            span = (r.last_ns - r.first_ns) / 1e3
+            gap = (r.first_ns - records[i - 1].last_ns) / 1e3 if i else 0.0
+            ns = r.cta0_exit_ns - r.cta0_entry_ns
+            mhz = (r.cta0_exit_clock - r.cta0_entry_clock) / ns * 1e3 if ns > 0 else None
+            rows.append({"kind": kind, "span_us": span, "gap_before_us": gap, "sm_mhz": mhz,
+                         # CTA 0 from its entry to its exit; the rest of the span is the
+                         # launch skew of later CTAs plus the tail of the last ones
+                         "cta0_us": ns / 1e3,
+                         "cycles": span * mhz if mhz else 0.0})
+        summary = {}
+        for row in rows:
+            entry = summary.setdefault(row["kind"], {"launches": 0, "span_us": 0.0,
+                                                     "gap_before_us": 0.0, "cta0_us": 0.0,
+                                                     "mcycles": 0.0, "mhz": []})
+            entry["launches"] += 1
+            entry["span_us"] += row["span_us"]
+            entry["gap_before_us"] += row["gap_before_us"]
+            entry["cta0_us"] += row["cta0_us"]
+            entry["mcycles"] += row["cycles"] / 1e6
+            if row["sm_mhz"]:
+                entry["mhz"].append(row["sm_mhz"])
+        for entry in summary.values():
+            mhz = entry.pop("mhz")
+            entry["sm_mhz_mean"] = sum(mhz) / len(mhz) if mhz else None
+        total = (records[-1].last_ns - records[0].first_ns) / 1e3
+        spans = sum(r["span_us"] for r in rows)
+        gaps = sum(r["gap_before_us"] for r in rows)
+        return {"pass_us": total, "kernel_spans_us": spans, "gaps_us": gaps,
+                "gaps_per_launch_us": gaps / max(len(rows) - 1, 1), "by_kind": summary}
+
+    for _ in range(5):
+        model.forward_graph(images, logits, batch, stream)
+    graph = capture(lambda: model.forward_graph(images, logits, batch, stream), 1)
+    profiled_ms = {}
+    profiled = capture(lambda: profiled_ms.setdefault(
+        "records", model.forward_profiled(images, logits, batch, stream)), 1)
+    event_us = sum(r["ms"] for r in profiled_ms["records"]) * 1e3
+    cuvit.kernels.device_status()
+    line = {"mode": "timeline", "workload": f"{label} {precision_name.upper()}, batch {batch}",
+            "launches_per_pass": per_pass, "graph_replay": analyse(graph),
+            "profiled_pass": dict(analyse(profiled), event_sum_us=event_us)}
+    print(json.dumps(line), flush=True)
+    model.close()
+
+
 def main() -> None:
     args = parse_args()
-    if args.impl == "reference":
+    if args.timeline:
+        os.environ["CUVIT_LIBRARY_VARIANT"] = "timeline"
+        timeline_arm(args)
+    elif args.impl == "reference":
         reference_arm(args)
     else:
         our_arm(args)

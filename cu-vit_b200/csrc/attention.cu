@@ -62,6 +62,7 @@ __global__ void __launch_bounds__(kThreads)
     attention_kernel(const __grid_constant__ CUtensorMap map_q,
                      const __grid_constant__ CUtensorMap map_kv,
                      const __grid_constant__ CUtensorMap map_v, const Params p) {
+    dev::timeline_enter();
     using L = Layout<ElemBytes>;
     using T = typename std::conditional<ElemBytes == 2, __nv_bfloat16, float>::type;
     constexpr dev::MmaKind kKind = ElemBytes == 2 ? dev::MmaKind::kF16 : dev::MmaKind::kTF32;
@@ -316,6 +317,7 @@ __global__ void __launch_bounds__(kThreads)
         dev::tc_fence_after();
         dev::tmem_dealloc(tmem, L::kTmemColumns);
     }
+    dev::timeline_exit();
 }
 
 // ---------------------------------------------------------------------------------------
@@ -370,6 +372,7 @@ __global__ void __launch_bounds__(kPipeThreads, 1)
     attention_bf16_pipelined(const __grid_constant__ CUtensorMap map_q,
                              const __grid_constant__ CUtensorMap map_kv,
                              const __grid_constant__ CUtensorMap map_ctx, const PipeParams p) {
+    dev::timeline_enter();
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw_base = dev::smem_u32(smem_raw);
     const uint32_t base = (raw_base + 1023u) & ~1023u;
@@ -722,6 +725,7 @@ __global__ void __launch_bounds__(kPipeThreads, 1)
         dev::tc_fence_after();
         dev::tmem_dealloc(tmem, 512);
     }
+    dev::timeline_exit();
 }
 
 // Where the second softmax warpgroup's keys begin and where O accumulates, for n_keys score

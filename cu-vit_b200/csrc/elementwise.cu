@@ -90,6 +90,7 @@ __global__ void __launch_bounds__(kThreads)
                            const float* __restrict__ gamma, const float* __restrict__ beta,
                            Out* __restrict__ output, long long out_stride, int rows, int columns,
                            float epsilon, int reverse) {
+    dev::timeline_enter();
     dev::grid_dependency_wait();
     dev::grid_launch_dependents();
     const int slot = blockIdx.x * kRowsPerBlock + threadIdx.x / kWarp;
@@ -140,6 +141,7 @@ __global__ void __launch_bounds__(kThreads)
             store4(out + 4 * v, y);
         }
     }
+    dev::timeline_exit();
 }
 
 __device__ float block_sum(float value, float* scratch) {
@@ -353,6 +355,7 @@ __global__ void broadcast_kernel(float* __restrict__ destination,
 __global__ void init_tokens_kernel(float* __restrict__ tokens, const float* __restrict__ cls,
                                    const float* __restrict__ pos, long long per_image,
                                    int embed, long long total, int vectorised) {
+    dev::timeline_enter();
     dev::grid_dependency_wait();
     dev::grid_launch_dependents();
     const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
@@ -376,6 +379,7 @@ __global__ void init_tokens_kernel(float* __restrict__ tokens, const float* __re
             tokens[i] = within < embed ? cls[within] + pos[within] : pos[within];
         }
     }
+    dev::timeline_exit();
 }
 
 __global__ void convert_bf16_kernel(const float* __restrict__ input,
@@ -405,6 +409,7 @@ template <typename Out, int Vec>
 __global__ void extract_patches_kernel(const float* __restrict__ images, Out* __restrict__ patches,
                                        int channels, int height, int width, int patch,
                                        int across, int per_image, long long total) {
+    dev::timeline_enter();
     dev::grid_dependency_wait();
     dev::grid_launch_dependents();
     const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
@@ -432,6 +437,7 @@ __global__ void extract_patches_kernel(const float* __restrict__ images, Out* __
             store1(patches + index, __ldg(images + source));
         }
     }
+    dev::timeline_exit();
 }
 
 // The same gather, one block per (image, row of patches): the block reads that strip of the
@@ -444,6 +450,7 @@ __global__ void __launch_bounds__(kThreads)
     extract_patch_rows_kernel(const In* __restrict__ images, Out* __restrict__ patches,
                               int channels, int height, int width, int patch, int across,
                               int patch_rows, int reverse) {
+    dev::timeline_enter();
     dev::grid_dependency_wait();
     dev::grid_launch_dependents();
     const int slot = static_cast<int>(blockIdx.x);
@@ -476,6 +483,7 @@ __global__ void __launch_bounds__(kThreads)
             *reinterpret_cast<uint2*>(target) = __ldg(reinterpret_cast<const uint2*>(source));
         }
     }
+    dev::timeline_exit();
 }
 
 // Top-k report (report_top, src/main.cpp:90-114), one warp per row: the row maximum and sum

@@ -37,6 +37,7 @@ __global__ void __launch_bounds__(kSimtThreads)
                      int count, int inner, long long stride_a, long long stride_b,
                      long long stride_c, long long outer_a, long long outer_b, long long outer_c,
                      int accumulate, int apply_gelu) {
+    dev::timeline_enter();
     dev::grid_dependency_wait();
     dev::grid_launch_dependents();
     __shared__ float tile_a[kSimtK][kSimtTile + 4];
@@ -143,6 +144,7 @@ __global__ void __launch_bounds__(kSimtThreads)
             }
         }
     }
+    dev::timeline_exit();
 }
 
 int launch_simt(const Resolved& r, cudaStream_t stream) {

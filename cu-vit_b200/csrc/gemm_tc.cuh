@@ -318,6 +318,7 @@ __global__ void __launch_bounds__(TcShape<ElemBytes, BN, Split>::kThreads, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tma_a,
                    const __grid_constant__ CUtensorMap tma_b,
                    const __grid_constant__ CUtensorMap tma_c, const TcParams p) {
+    dev::timeline_enter();
     using Shape = TcShape<ElemBytes, BN, Split>;
     constexpr int kStages = Shape::kStages;
     constexpr dev::MmaKind kKind = ElemBytes == 2 ? dev::MmaKind::kF16 : dev::MmaKind::kTF32;
@@ -633,6 +634,7 @@ __global__ void __launch_bounds__(TcShape<ElemBytes, BN, Split>::kThreads, 1)
         dev::tc_fence_after();
         dev::tmem_dealloc(tmem_base, Shape::kTmemColumns);
     }
+    dev::timeline_exit();
 }
 
 } // namespace cuvit::gemm

@@ -52,6 +52,7 @@ __global__ void __launch_bounds__(PairShape<BN>::kThreads, 1)
     tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap tma_a,
                         const __grid_constant__ CUtensorMap tma_b,
                         const __grid_constant__ CUtensorMap tma_c, const TcParams p) {
+    dev::timeline_enter();
     using Shape = PairShape<BN>;
     constexpr int kStages = Shape::kStages;
     constexpr uint32_t kIdesc = dev::make_idesc(1u, 2 * kBlockM, BN, false, false);
@@ -309,6 +310,7 @@ __global__ void __launch_bounds__(PairShape<BN>::kThreads, 1)
         dev::tc_fence_after();
         dev::tmem_dealloc_pair(tmem_base, Shape::kTmemColumns);
     }
+    dev::timeline_exit();
 }
 
 } // namespace cuvit::gemm

@@ -11,6 +11,8 @@
 
 #include <cstdint>
 
+#include "timeline.cuh"
+
 namespace cuvit::dev {
 
 // Device status word bits (read and cleared by cuvit_device_status()).

@@ -2,10 +2,12 @@
 
 #include "ptx.cuh"
 
+#include <algorithm>
 #include <atomic>
 #include <cstring>
 #include <mutex>
 #include <string>
+#include <vector>
 
 namespace cuvit::host {
 namespace {
@@ -203,6 +205,33 @@ int encode_tma(const TmaTensor& tensor, CUtensorMap* map) {
     return CUVIT_OK;
 }
 
+// ---- device timeline (instrumented builds only) ---------------------------------------------
+
+#ifdef CUVIT_TIMELINE
+namespace {
+std::mutex g_timeline_mutex;
+std::vector<int (*)(void*)>& timeline_binders() {
+    static std::vector<int (*)(void*)> binders;
+    return binders;
+}
+cuvit::dev::TimelineRecord* g_timeline_table = nullptr;
+
+__global__ void timeline_clear_kernel(cuvit::dev::TimelineRecord* records, int count) {
+    const int i = static_cast<int>(blockIdx.x * blockDim.x + threadIdx.x);
+    if (i < count) {
+        cuvit::dev::TimelineRecord empty{};
+        empty.first_ns = ~0ull;
+        records[i] = empty;
+    }
+}
+} // namespace
+
+void register_timeline_binder(int (*bind)(void* records)) {
+    std::lock_guard<std::mutex> lock(g_timeline_mutex);
+    timeline_binders().push_back(bind);
+}
+#endif
+
 } // namespace cuvit::host
 
 using namespace cuvit::host;
@@ -257,6 +286,83 @@ int cuvit_device_status(unsigned* flags) {
 }
 
 long long cuvit_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
+
+int cuvit_timeline_available(void) {
+#ifdef CUVIT_TIMELINE
+    return 1;
+#else
+    return 0;
+#endif
+}
+
+int cuvit_timeline_reset(void) {
+#ifndef CUVIT_TIMELINE
+    return fail(CUVIT_UNSUPPORTED, "this build has no device timeline (build with --timeline)");
+#else
+    const DeviceContext* context = nullptr;
+    CUVIT_TRY(current_context(&context));
+    std::lock_guard<std::mutex> lock(g_timeline_mutex);
+    CUVIT_TRY_CUDA(cudaDeviceSynchronize());
+    if (g_timeline_table == nullptr) {
+        CUVIT_TRY_CUDA(cudaMalloc(&g_timeline_table,
+                                  sizeof(cuvit::dev::TimelineRecord) * cuvit::dev::kTimelineSlots));
+        for (int (*bind)(void*) : timeline_binders()) {
+            if (bind(g_timeline_table) != 0) {
+                return fail(CUVIT_CUDA_ERROR, "binding the device timeline table failed");
+            }
+        }
+    }
+    timeline_clear_kernel<<<(cuvit::dev::kTimelineSlots + 255) / 256, 256>>>(
+        g_timeline_table, cuvit::dev::kTimelineSlots);
+    CUVIT_TRY_CUDA(cudaGetLastError());
+    CUVIT_TRY_CUDA(cudaDeviceSynchronize());
+    return CUVIT_OK;
+#endif
+}
+
+int cuvit_timeline_read(cuvit_timeline_record* records, int capacity, int* count) {
+#ifndef CUVIT_TIMELINE
+    (void)records;
+    (void)capacity;
+    (void)count;
+    return fail(CUVIT_UNSUPPORTED, "this build has no device timeline (build with --timeline)");
+#else
+    if (count == nullptr || (records == nullptr && capacity > 0)) {
+        return fail(CUVIT_INVALID_ARGUMENT, "timeline output cannot be null");
+    }
+    std::lock_guard<std::mutex> lock(g_timeline_mutex);
+    if (g_timeline_table == nullptr) {
+        return fail(CUVIT_INVALID_ARGUMENT, "cuvit_timeline_reset() has not been called");
+    }
+    CUVIT_TRY_CUDA(cudaDeviceSynchronize());
+    std::vector<cuvit::dev::TimelineRecord> table(cuvit::dev::kTimelineSlots);
+    CUVIT_TRY_CUDA(cudaMemcpy(table.data(), g_timeline_table,
+                              sizeof(cuvit::dev::TimelineRecord) * table.size(),
+                              cudaMemcpyDeviceToHost));
+    std::vector<cuvit::dev::TimelineRecord> used;
+    for (const auto& r : table) {
+        if (r.grid != 0) {
+            used.push_back(r);
+        }
+    }
+    std::sort(used.begin(), used.end(),
+              [](const auto& a, const auto& b) { return a.first_ns < b.first_ns; });
+    *count = static_cast<int>(used.size());
+    for (int i = 0; i < capacity && i < *count; ++i) {
+        const auto& r = used[static_cast<size_t>(i)];
+        cuvit_timeline_record& out = records[i];
+        out.grid = r.grid - 1;
+        out.first_ns = r.first_ns;
+        out.last_ns = r.last_ns;
+        out.warps = r.warps;
+        out.cta0_entry_ns = r.cta0_ns[0];
+        out.cta0_exit_ns = r.cta0_ns[1];
+        out.cta0_entry_clock = r.cta0_clock[0];
+        out.cta0_exit_clock = r.cta0_clock[1];
+    }
+    return CUVIT_OK;
+#endif
+}
 
 int cuvit_selftest_bounded_wait(unsigned long long limit_ns) {
     if (limit_ns == 0 || limit_ns > 1000000000ull) {

@@ -7,10 +7,15 @@ There is no fallback: if the library is missing, every entry point raises.
 from __future__ import annotations
 
 import ctypes
+import os
 import pathlib
 import threading
 
-LIBRARY_PATH = pathlib.Path(__file__).resolve().parent / "_lib" / "libcuvit_b200.so"
+# CUVIT_LIBRARY_VARIANT=timeline loads the diagnostic build whose kernels stamp a device
+# timeline (cu-vit_b200/build.py --timeline); anything else loads the product library.
+LIBRARY_PATH = pathlib.Path(__file__).resolve().parent / "_lib" / (
+    "libcuvit_b200_timeline.so" if os.environ.get("CUVIT_LIBRARY_VARIANT") == "timeline"
+    else "libcuvit_b200.so")
 
 OK = 0
 INVALID_ARGUMENT = 1
@@ -87,6 +92,12 @@ class LaunchRecordC(ctypes.Structure):
     ]
 
 
+class TimelineRecordC(ctypes.Structure):
+    _fields_ = [(name, ctypes.c_ulonglong) for name in (
+        "grid", "first_ns", "last_ns", "warps", "cta0_entry_ns", "cta0_exit_ns",
+        "cta0_entry_clock", "cta0_exit_clock")]
+
+
 LAUNCH_KINDS = ["patches", "tokens", "gemm_patch", "layer_norm", "gemm_qkv", "attention",
                 "gemm_proj", "gemm_fc1", "gemm_fc2", "gemm_head"]
 
@@ -153,6 +164,9 @@ SIGNATURES = {
     "cuvit_vit_image_elements": (_sz, [_vp]),
     "cuvit_vit_host_image_bytes": (_sz, [_vp]),
     "cuvit_vit_launches_per_forward": (_i, [_vp, _i]),
+    "cuvit_timeline_available": (_i, []),
+    "cuvit_timeline_reset": (_i, []),
+    "cuvit_timeline_read": (_i, [ctypes.POINTER(TimelineRecordC), _i, ctypes.POINTER(_i)]),
 }
 
 _lock = threading.Lock()

@@ -254,6 +254,31 @@ int cuvit_selftest_bounded_wait(unsigned long long limit_ns);
 /* Number of kernels this library launched from the calling process (all threads). */
 long long cuvit_launch_count(void);
 
+/* Device timeline (diagnostic; no reference counterpart). Only the instrumented variant of
+ * the library (built with `python cu-vit_b200/build.py --timeline`, file
+ * libcuvit_b200_timeline.so) records it; elsewhere cuvit_timeline_available() returns 0 and
+ * the other two calls return CUVIT_UNSUPPORTED. Each forward-path kernel stamps the global
+ * nanosecond timer when its first CTA starts and when its last CTA ends, and CTA 0 also
+ * records its SM's cycle counter at entry and exit (cycles / ns = the SM clock that kernel
+ * ran at). One record per launch, keyed by the launch's grid id, current device only. */
+typedef struct cuvit_timeline_record {
+    unsigned long long grid;        /* per-launch grid identifier */
+    unsigned long long first_ns;    /* earliest CTA entry (global timer, ns) */
+    unsigned long long last_ns;     /* latest warp exit */
+    unsigned long long warps;       /* CTAs that stamped their exit (the grid's last ones) */
+    unsigned long long cta0_entry_ns;
+    unsigned long long cta0_exit_ns;
+    unsigned long long cta0_entry_clock; /* SM cycle counter of CTA 0 */
+    unsigned long long cta0_exit_clock;
+} cuvit_timeline_record;
+
+int cuvit_timeline_available(void);
+/* Synchronizes the device and clears the table (allocating it on first use). */
+int cuvit_timeline_reset(void);
+/* Synchronizes the device and returns the recorded launches in start order: up to capacity
+ * records, *count receives how many there are. */
+int cuvit_timeline_read(cuvit_timeline_record* records, int capacity, int* count);
+
 /* ---------------------------------------------------------------------------------------
  * Model runner. Replaces cuvit::VisionTransformer (include/cuvit/vit.hpp:63-120,
  * src/model/vit.cu:69-344): weights and activations live in two arenas allocated at
