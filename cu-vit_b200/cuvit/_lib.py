@@ -92,6 +92,11 @@ class LaunchRecordC(ctypes.Structure):
     ]
 
 
+class PreprocessingC(ctypes.Structure):
+    _fields_ = [("size", ctypes.c_int), ("crop_fraction", ctypes.c_float),
+                ("mean", ctypes.c_float * 3), ("stddev", ctypes.c_float * 3)]
+
+
 class TimelineRecordC(ctypes.Structure):
     _fields_ = [(name, ctypes.c_ulonglong) for name in (
         "grid", "first_ns", "last_ns", "warps", "cta0_entry_ns", "cta0_exit_ns",
@@ -164,6 +169,22 @@ SIGNATURES = {
     "cuvit_vit_image_elements": (_sz, [_vp]),
     "cuvit_vit_host_image_bytes": (_sz, [_vp]),
     "cuvit_vit_launches_per_forward": (_i, [_vp, _i]),
+    "cuvit_preprocessing_default": (None, [ctypes.POINTER(PreprocessingC)]),
+    "cuvit_preprocess": (_i, [_vp, _i, _i, _i, ctypes.c_int64, ctypes.POINTER(PreprocessingC),
+                              _vp, _vp]),
+    "cuvit_shard": (_i, [_i, _i, _i, ctypes.POINTER(_i), ctypes.POINTER(_i)]),
+    "cuvit_comm_unique_id": (_i, [_vp, _sz]),
+    "cuvit_comm_create": (_i, [_vp, _i, _i, _i, ctypes.POINTER(_vp)]),
+    "cuvit_comm_destroy": (_i, [_vp]),
+    "cuvit_gather_logits": (_i, [_vp, _vp, _vp, _i, _i, _i, _vp]),
+    "cuvit_replicas_create": (
+        _i, [ctypes.POINTER(VitConfigC), ctypes.POINTER(_vp), _i, _i, _i, ctypes.POINTER(_i), _i,
+             ctypes.POINTER(_vp)]
+    ),
+    "cuvit_replicas_destroy": (_i, [_vp]),
+    "cuvit_replicas_device_count": (_i, [_vp]),
+    "cuvit_replicas_forward_host": (_i, [_vp, _vp, _vp, _i]),
+    "cuvit_replicas_forward": (_i, [_vp, _vp, _i, _vp, _i, _i]),
     "cuvit_timeline_available": (_i, []),
     "cuvit_timeline_reset": (_i, []),
     "cuvit_timeline_read": (_i, [ctypes.POINTER(TimelineRecordC), _i, ctypes.POINTER(_i)]),

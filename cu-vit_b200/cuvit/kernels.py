@@ -215,6 +215,18 @@ def launch_attention(qkv, context, dtype: int, batch: int, tokens: int, heads: i
                                          head_dim, scale, _stream(stream)))
 
 
+def launch_preprocess(pixels, tensor, batch: int, width: int, height: int, size: int = 224,
+                      crop_fraction: float = 0.9, mean=(0.5, 0.5, 0.5), stddev=(0.5, 0.5, 0.5),
+                      image_stride: int = 0, stream=None) -> None:
+    """Device preprocessing (replaces cuvit::preprocess, src/runtime/image.cpp:90-135):
+    `batch` interleaved uint8 RGB images -> planar float [batch, 3, size, size]."""
+    settings = _lib.PreprocessingC(size, crop_fraction, (ctypes.c_float * 3)(*mean),
+                                   (ctypes.c_float * 3)(*stddev))
+    check(_lib.library().cuvit_preprocess(_ptr(pixels), batch, width, height, image_stride,
+                                          ctypes.byref(settings), _ptr(tensor),
+                                          _stream(stream)))
+
+
 def device_status() -> int:
     """Synchronises the current device, returns and clears its status bits (raises on a
     device-side timeout)."""

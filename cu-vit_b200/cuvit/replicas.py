@@ -1,13 +1,24 @@
-"""Data-parallel replicas: one process per GPU, the batch sharded by image, weights
-replicated, and the logits gathered to rank 0 -- the only collective of the path (images never
-interact, so nothing is exchanged per layer).
+"""Data-parallel replicas: the batch sharded by image, weights replicated, and the logits
+gathered to one place -- the only exchange of the path (images never interact, so nothing is
+exchanged per layer).
 
-The helpers work on any torch.distributed backend (NCCL on GPUs, gloo on CPU for tests).
+Two layers:
+  * the C ABI's multi-GPU entry points (no torch): `shard_c` (cuvit_shard), `Comm` (an NCCL
+    communicator for one process per GPU, with `gather_logits` to a root rank) and `Replicas`
+    (one process driving several GPUs, one host thread per device);
+  * torch.distributed helpers for the host side of a multi-process job (CPU affinity, and a
+    gloo/NCCL logits gather used by the CPU tests of the sharding logic).
 """
 
 from __future__ import annotations
 
+import ctypes
 import os
+
+import numpy as np
+
+from . import _lib
+from .errors import check
 
 SYSFS_PCI_DEVICES = "/sys/bus/pci/devices"
 
@@ -110,3 +121,127 @@ def gather_logits(local, world: int, rank: int, counts: list[int] | None = None)
     if rank != 0:
         return None
     return torch.cat([buffers[r][: counts[r]] for r in range(world)])
+
+
+# ---- the C ABI ------------------------------------------------------------------------------
+
+def _ptr(value) -> ctypes.c_void_p:
+    if value is None:
+        return ctypes.c_void_p(0)
+    if hasattr(value, "data_ptr"):
+        return ctypes.c_void_p(value.data_ptr())
+    if isinstance(value, np.ndarray):
+        return ctypes.c_void_p(value.ctypes.data)
+    return ctypes.c_void_p(int(value))
+
+
+def _stream(stream) -> ctypes.c_void_p:
+    if stream is None:
+        return ctypes.c_void_p(0)
+    if hasattr(stream, "cuda_stream"):
+        return ctypes.c_void_p(stream.cuda_stream)
+    return ctypes.c_void_p(int(stream))
+
+
+def shard_c(total: int, parts: int, index: int) -> tuple[int, int]:
+    """cuvit_shard: (first, count) of part `index` -- the C library's own partition, which
+    the multi-GPU entry points use."""
+    first, count = ctypes.c_int(0), ctypes.c_int(0)
+    check(_lib.library().cuvit_shard(total, parts, index, ctypes.byref(first),
+                                     ctypes.byref(count)))
+    return first.value, count.value
+
+
+class Comm:
+    """An NCCL communicator through the C ABI (one process per GPU). Rank 0 calls
+    `unique_id()` and hands the bytes to every rank by any host channel."""
+
+    ID_BYTES = 128
+
+    @staticmethod
+    def unique_id() -> bytes:
+        buffer = ctypes.create_string_buffer(Comm.ID_BYTES)
+        check(_lib.library().cuvit_comm_unique_id(buffer, Comm.ID_BYTES))
+        return buffer.raw
+
+    def __init__(self, unique_id: bytes, world: int, rank: int, device: int):
+        if len(unique_id) != Comm.ID_BYTES:
+            raise ValueError(f"a unique id has {Comm.ID_BYTES} bytes")
+        handle = ctypes.c_void_p(0)
+        buffer = ctypes.create_string_buffer(unique_id, Comm.ID_BYTES)
+        check(_lib.library().cuvit_comm_create(buffer, world, rank, device,
+                                               ctypes.byref(handle)))
+        self._handle = handle
+        self.world, self.rank, self.device = world, rank, device
+
+    def gather_logits(self, local, gathered, rows: int, classes: int, root: int = 0,
+                      stream=None) -> None:
+        """cuvit_gather_logits: every rank's [rows, classes] device logits into `gathered`
+        (device, root only) in rank order."""
+        check(_lib.library().cuvit_gather_logits(self._handle, _ptr(local), _ptr(gathered),
+                                                 rows, classes, root, _stream(stream)))
+
+    def close(self) -> None:
+        if getattr(self, "_handle", None):
+            check(_lib.library().cuvit_comm_destroy(self._handle))
+            self._handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:  # interpreter shutdown
+            pass
+
+
+class Replicas:
+    """One process, several GPUs (cuvit_replicas_*): a model per device, one host thread per
+    device, shards in cuvit_shard order."""
+
+    def __init__(self, config, weights, max_batch_per_device: int, precision: int,
+                 devices: list[int]):
+        from .vit import host_tensors
+
+        self.config = config
+        arrays = host_tensors(config, weights)
+        pointers = (ctypes.c_void_p * len(arrays))(*[a.ctypes.data for a in arrays])
+        c_devices = (ctypes.c_int * len(devices))(*devices)
+        c_config = config.to_c()
+        handle = ctypes.c_void_p(0)
+        check(_lib.library().cuvit_replicas_create(ctypes.byref(c_config), pointers,
+                                                   len(arrays), max_batch_per_device,
+                                                   precision, c_devices, len(devices),
+                                                   ctypes.byref(handle)))
+        self._handle = handle
+        self.devices = list(devices)
+
+    def device_count(self) -> int:
+        return _lib.library().cuvit_replicas_device_count(self._handle)
+
+    def forward_host(self, images: np.ndarray) -> np.ndarray:
+        """Host images in, host logits [batch, classes] out (synchronous)."""
+        images = np.ascontiguousarray(images, dtype=np.float32).reshape(-1)
+        per_image = self.config.image_elements()
+        if images.size % per_image:
+            raise ValueError("image buffer is not a whole number of images")
+        batch = images.size // per_image
+        logits = np.empty((batch, self.config.classes), np.float32)
+        check(_lib.library().cuvit_replicas_forward_host(self._handle, _ptr(images),
+                                                         _ptr(logits), batch))
+        return logits
+
+    def forward(self, images, images_device: int, logits, logits_device: int,
+                batch: int) -> None:
+        """Device-resident images and logits (synchronous)."""
+        check(_lib.library().cuvit_replicas_forward(self._handle, _ptr(images), images_device,
+                                                    _ptr(logits), logits_device, batch))
+
+    def close(self) -> None:
+        if getattr(self, "_handle", None):
+            check(_lib.library().cuvit_replicas_destroy(self._handle))
+            self._handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:  # interpreter shutdown
+            pass

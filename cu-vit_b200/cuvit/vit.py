@@ -113,6 +113,24 @@ def random_weights(config: VitConfig, seed: int, std: float = 0.02) -> dict[str,
     return weights
 
 
+def host_tensors(config: VitConfig, weights) -> list[np.ndarray]:
+    """The model's tensors as contiguous float32 arrays in load order, from a dict name ->
+    array or a cvw.WeightFile; names and shapes are checked against config."""
+    arrays = []
+    for name, extents in tensor_specs(config):
+        if hasattr(weights, "float_data"):
+            data = weights.float_data(name, extents)
+        else:
+            if name not in weights:
+                raise RuntimeError(f"Weight file has no tensor named '{name}'")
+            data = np.asarray(weights[name], dtype=np.float32)
+            if tuple(data.shape) != tuple(extents):
+                raise RuntimeError(f"Tensor '{name}' has shape {list(data.shape)}, but "
+                                   f"{list(extents)} was expected")
+        arrays.append(np.ascontiguousarray(data, dtype=np.float32))
+    return arrays
+
+
 class VisionTransformer:
     """reference: cuvit::VisionTransformer (include/cuvit/vit.hpp:63-120).
 
@@ -126,21 +144,7 @@ class VisionTransformer:
         lib = _lib.library()
         c_config = config.to_c()
         check(lib.cuvit_vit_config_validate(ctypes.byref(c_config)))
-        arrays = []
-        for name, extents in tensor_specs(config):
-            if hasattr(weights, "float_data"):
-                data = weights.float_data(name, extents)
-            else:
-                if name not in weights:
-                    raise RuntimeError(f"Weight file has no tensor named '{name}'")
-                data = np.asarray(weights[name], dtype=np.float32)
-                if tuple(data.shape) != tuple(extents) and data.size != int(np.prod(extents)):
-                    raise RuntimeError(f"Tensor '{name}' has shape {list(data.shape)}, but "
-                                       f"{list(extents)} was expected")
-                if tuple(data.shape) != tuple(extents):
-                    raise RuntimeError(f"Tensor '{name}' has shape {list(data.shape)}, but "
-                                       f"{list(extents)} was expected")
-            arrays.append(np.ascontiguousarray(data, dtype=np.float32))
+        arrays = host_tensors(config, weights)
         pointers = (ctypes.c_void_p * len(arrays))(*[a.ctypes.data for a in arrays])
         handle = ctypes.c_void_p(0)
         check(lib.cuvit_vit_create_from_host(ctypes.byref(c_config), pointers, len(arrays),

@@ -219,6 +219,32 @@ int cuvit_logits_top_k(const float* logits, int batch, int classes, int k, int* 
                        float* values, float* probabilities, cuvit_stream_t stream);
 
 /* ---------------------------------------------------------------------------------------
+ * Image preprocessing on the device. Replaces cuvit::preprocess (include/cuvit/image.hpp,
+ * src/runtime/image.cpp:90-135), which the reference runs on the host: the shorter side is
+ * resized to round(size / crop_fraction) with bilinear sampling and edge clamping, the centre
+ * size x size square kept, values scaled to [0, 1] and normalised per channel. Results are
+ * bit-identical to the reference's host code.
+ * ------------------------------------------------------------------------------------- */
+typedef struct cuvit_preprocessing {
+    int size;            /* output side (reference default 224) */
+    float crop_fraction; /* in (0, 1] (default 0.9) */
+    float mean[3];       /* per channel (default 0.5) */
+    float stddev[3];     /* per channel, nonzero (default 0.5) */
+} cuvit_preprocessing;
+
+/* The reference's Preprocessing defaults (include/cuvit/image.hpp). */
+void cuvit_preprocessing_default(cuvit_preprocessing* settings);
+
+/* pixels: device, `batch` interleaved 8-bit RGB images of width x height, image_stride bytes
+ * apart (0 = packed, width * height * 3). tensor: device float [batch, 3, size, size], the
+ * layout cuvit_vit_forward reads. Rejects what the reference rejects (empty image, size <= 0,
+ * crop fraction outside (0, 1], a zero deviation) with CUVIT_INVALID_ARGUMENT and its
+ * message, before any launch. */
+int cuvit_preprocess(const uint8_t* pixels, int batch, int width, int height,
+                     int64_t image_stride, const cuvit_preprocessing* settings, float* tensor,
+                     cuvit_stream_t stream);
+
+/* ---------------------------------------------------------------------------------------
  * Fused attention. Replaces the Q.K^T GEMM -> launch_softmax -> .V GEMM sequence of
  * src/model/vit.cu:198-242 with one kernel that keeps the T x T logits on chip.
  *
@@ -394,6 +420,51 @@ size_t cuvit_vit_image_elements(const cuvit_vit* model);
 size_t cuvit_vit_host_image_bytes(const cuvit_vit* model);
 /* Kernel launches one forward pass issues for this batch size. */
 int cuvit_vit_launches_per_forward(const cuvit_vit* model, int batch);
+
+/* ---------------------------------------------------------------------------------------
+ * Several GPUs. No reference counterpart: the reference runs one VisionTransformer on one
+ * device. Images are independent, so a batch shards by image across GPUs with the weights
+ * replicated, and the logits are the only data exchanged (no per-layer collective).
+ * ------------------------------------------------------------------------------------- */
+
+/* The contiguous shard [*first, *first + *count) of `total` images owned by part `index` of
+ * `parts`: the first total % parts parts take one extra image. Gathering the parts in index
+ * order restores the global image order. */
+int cuvit_shard(int total, int parts, int index, int* first, int* count);
+
+/* One process per GPU: an NCCL communicator (NCCL is loaded at run time; these calls return
+ * CUVIT_UNSUPPORTED where libnccl.so.2 cannot be loaded). Rank 0 makes the unique id
+ * (id_capacity >= 128 bytes) and hands it to every rank by any host channel; every rank then
+ * calls cuvit_comm_create, which returns once all `world` ranks have joined. */
+typedef struct cuvit_comm cuvit_comm;
+int cuvit_comm_unique_id(void* id, size_t id_capacity);
+int cuvit_comm_create(const void* id, int world, int rank, int device, cuvit_comm** comm);
+int cuvit_comm_destroy(cuvit_comm* comm);
+/* Gathers every rank's [rows, classes] device logits to `root` (grouped NCCL send / receive,
+ * queued on `stream`): gathered (root only, device) receives world * rows rows in rank order.
+ * Every rank calls it with the same rows, classes and root, in the same order relative to its
+ * other collectives. */
+int cuvit_gather_logits(cuvit_comm* comm, const float* local, float* gathered, int rows,
+                        int classes, int root, cuvit_stream_t stream);
+
+/* One process driving several GPUs: a model per device (weights uploaded to each), one host
+ * thread per device. devices may repeat a device (two replicas sharing one GPU). */
+typedef struct cuvit_replicas cuvit_replicas;
+int cuvit_replicas_create(const cuvit_vit_config* config, const float* const* tensors,
+                          int tensor_count, int max_batch_per_device, int precision,
+                          const int* devices, int device_count, cuvit_replicas** replicas);
+int cuvit_replicas_destroy(cuvit_replicas* replicas);
+int cuvit_replicas_device_count(const cuvit_replicas* replicas);
+/* Host images [batch, C, H, W] in, host logits [batch, classes] out, synchronous: device i
+ * runs shard i (cuvit_shard) through cuvit_vit_forward_host and writes its rows of the
+ * logits. batch <= device_count * max_batch_per_device. */
+int cuvit_replicas_forward_host(cuvit_replicas* replicas, const float* images, float* logits,
+                                int batch);
+/* Device-resident form: images on device images_device, logits into a buffer on device
+ * logits_device; device i copies its shard of the images peer to peer, replays its pass and
+ * copies its logits peer to peer into their rows. Synchronous. */
+int cuvit_replicas_forward(cuvit_replicas* replicas, const float* images, int images_device,
+                           float* logits, int logits_device, int batch);
 
 #if defined(__GNUC__)
 #pragma GCC visibility pop

@@ -68,6 +68,8 @@ def lib() -> ctypes.CDLL:
     library.oracle_vit_forward_batch.argtypes = [ctypes.c_void_p, _f, ctypes.c_void_p,
                                                  ctypes.c_void_p, _i, ctypes.c_void_p, _i]
     library.oracle_max_threads.restype = _i
+    library.oracle_preprocess.restype = _i
+    library.oracle_preprocess.argtypes = [ctypes.c_void_p, _i, _i, _i, _f, _f32p, _f32p, _f32p]
     return library
 
 
@@ -190,6 +192,33 @@ def vit_forward(config, weights: dict, specs, images, threads: int = 0) -> np.nd
     return logits
 
 
+def preprocess(pixels, size: int = 224, crop_fraction: float = 0.9, mean=(0.5, 0.5, 0.5),
+               stddev=(0.5, 0.5, 0.5)) -> np.ndarray:
+    """preprocess (src/runtime/image.cpp:90-135) of one interleaved uint8 RGB image [H, W, 3]
+    into a planar float32 [3, size, size] tensor."""
+    pixels = np.ascontiguousarray(pixels, dtype=np.uint8)
+    height, width = pixels.shape[:2]
+    out = np.empty(3 * size * size, np.float32)
+    status = lib().oracle_preprocess(pixels.ctypes.data, width, height, size, crop_fraction,
+                                     _f32(mean), _f32(stddev), out)
+    if status != 0:
+        raise ValueError("preprocessing arguments rejected")
+    return out.reshape(3, size, size)
+
+
+def ref_preprocess(pixels, size: int = 224, crop_fraction: float = 0.9, mean=(0.5, 0.5, 0.5),
+                   stddev=(0.5, 0.5, 0.5)) -> np.ndarray:
+    """The reference's own cuvit::preprocess (oracle/_ref), same contract as preprocess()."""
+    pixels = np.ascontiguousarray(pixels, dtype=np.uint8)
+    height, width = pixels.shape[:2]
+    out = np.empty(3 * size * size, np.float32)
+    status = ref_cpu().ref_preprocess(pixels.ctypes.data, width, height, size, crop_fraction,
+                                      _f32(mean), _f32(stddev), out)
+    if status != 0:
+        raise ValueError("the reference rejected the preprocessing arguments")
+    return out.reshape(3, size, size)
+
+
 def max_threads() -> int:
     return int(lib().oracle_max_threads())
 
@@ -210,6 +239,8 @@ def ref_cpu() -> ctypes.CDLL:
     library.ref_vit_forward.argtypes = [ctypes.c_char_p, ctypes.c_void_p, _f, ctypes.c_void_p,
                                         _i, ctypes.c_void_p, _i]
     library.ref_vit_forward.restype = _i
+    library.ref_preprocess.argtypes = [ctypes.c_void_p, _i, _i, _i, _f, _f32p, _f32p, _f32p]
+    library.ref_preprocess.restype = _i
     return library
 
 

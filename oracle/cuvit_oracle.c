@@ -429,3 +429,64 @@ int oracle_vit_forward_batch(const int* config_ints, float epsilon, const float*
 }
 
 int oracle_max_threads(void) { return (int)sysconf(_SC_NPROCESSORS_ONLN); }
+
+/* Image preprocessing: src/runtime/image.cpp:90-135 (preprocess) with its bilinear sampler
+ * image.cpp:39-56. The shorter side is resized to round(size / crop_fraction), the centre
+ * size x size square is kept, and both steps fold into one sampling pass that maps each
+ * output pixel back to a source coordinate; the sample is scaled to [0, 1] and normalised.
+ * Interleaved 8-bit RGB in, planar float [3, size, size] out. Every float operation is kept in
+ * the reference's order (no contraction). Returns 0, or -1 for arguments the reference
+ * rejects (empty image, size <= 0, crop fraction outside (0, 1], zero deviation). */
+static float oracle_pixel(const uint8_t* pixels, int width, int height, int column, int row,
+                          int channel) {
+    column = column < 0 ? 0 : (column > width - 1 ? width - 1 : column);
+    row = row < 0 ? 0 : (row > height - 1 ? height - 1 : row);
+    return (float)pixels[((size_t)row * (size_t)width + (size_t)column) * 3 + (size_t)channel];
+}
+
+static float oracle_bilinear(const uint8_t* pixels, int width, int height, float x, float y,
+                             int channel) {
+    const int left = (int)floorf(x);
+    const int top = (int)floorf(y);
+    const float dx = x - (float)left;
+    const float dy = y - (float)top;
+    const float top_edge = oracle_pixel(pixels, width, height, left, top, channel) * (1.0F - dx) +
+                           oracle_pixel(pixels, width, height, left + 1, top, channel) * dx;
+    const float bottom_edge =
+        oracle_pixel(pixels, width, height, left, top + 1, channel) * (1.0F - dx) +
+        oracle_pixel(pixels, width, height, left + 1, top + 1, channel) * dx;
+    return top_edge * (1.0F - dy) + bottom_edge * dy;
+}
+
+int oracle_preprocess(const uint8_t* pixels, int width, int height, int size,
+                      float crop_fraction, const float* mean, const float* stddev, float* out) {
+    if (pixels == NULL || width <= 0 || height <= 0 || size <= 0 || !(crop_fraction > 0.0F) ||
+        crop_fraction > 1.0F) {
+        return -1;
+    }
+    for (int channel = 0; channel < 3; ++channel) {
+        if (stddev[channel] == 0.0F) {
+            return -1;
+        }
+    }
+    const float resized = roundf((float)size / crop_fraction);
+    const int shorter = width < height ? width : height;
+    const float scale = (float)shorter / resized;
+    const float crop = (float)size * scale;
+    const float origin_x = ((float)width - crop) * 0.5F;
+    const float origin_y = ((float)height - crop) * 0.5F;
+    const float step = crop / (float)size;
+    const size_t plane = (size_t)size * (size_t)size;
+    for (int channel = 0; channel < 3; ++channel) {
+        for (int row = 0; row < size; ++row) {
+            for (int column = 0; column < size; ++column) {
+                const float x = origin_x + ((float)column + 0.5F) * step - 0.5F;
+                const float y = origin_y + ((float)row + 0.5F) * step - 0.5F;
+                const float value = oracle_bilinear(pixels, width, height, x, y, channel) / 255.0F;
+                out[(size_t)channel * plane + (size_t)row * (size_t)size + (size_t)column] =
+                    (value - mean[channel]) / stddev[channel];
+            }
+        }
+    }
+    return 0;
+}

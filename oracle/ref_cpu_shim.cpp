@@ -3,6 +3,7 @@
 // Cu-Vit), compiled from the reference sources in place by oracle/Makefile into
 // oracle/_ref/libcuvit_ref_cpu.so. It validates the C restatement in cuvit_oracle.c and
 // serves as the timed CPU baseline ("reference" kind).
+#include "cuvit/image.hpp"
 #include "cuvit/vit.hpp"
 #include "cuvit/weights.hpp"
 #include "reference/linear_algebra.hpp"
@@ -72,6 +73,35 @@ __attribute__((visibility("default"))) void ref_softmax(const float* input, floa
 __attribute__((visibility("default"))) void ref_gelu(const float* input, float* output,
                                                      int64_t count) {
     cuvit::reference::gelu(input, output, static_cast<size_t>(count));
+}
+
+// cuvit::preprocess (src/runtime/image.cpp:90-135) of one interleaved 8-bit RGB image into a
+// planar [3, size, size] tensor. Returns 0, or -1 when the reference throws.
+__attribute__((visibility("default"))) int ref_preprocess(const uint8_t* pixels, int width,
+                                                          int height, int size,
+                                                          float crop_fraction,
+                                                          const float* mean,
+                                                          const float* stddev, float* out) {
+    try {
+        cuvit::RgbImage image;
+        image.width = width;
+        image.height = height;
+        image.pixels.assign(pixels, pixels + static_cast<size_t>(width) * height * 3);
+        cuvit::Preprocessing settings;
+        settings.size = size;
+        settings.crop_fraction = crop_fraction;
+        for (int c = 0; c < 3; ++c) {
+            settings.mean[static_cast<size_t>(c)] = mean[c];
+            settings.stddev[static_cast<size_t>(c)] = stddev[c];
+        }
+        const std::vector<float> tensor = cuvit::preprocess(image, settings);
+        for (size_t i = 0; i < tensor.size(); ++i) {
+            out[i] = tensor[i];
+        }
+        return 0;
+    } catch (const std::exception&) {
+        return -1;
+    }
 }
 
 // Runs VitReference::forward over count images with `threads` worker threads, loading the

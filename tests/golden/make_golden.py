@@ -115,6 +115,25 @@ VIT_CASES = [
 ]
 
 
+# Image preprocessing (src/runtime/image.cpp:90-135): (label, height, width, size,
+# crop_fraction, mean, stddev, seed). Landscape, square, portrait, a single pixel (every tap
+# clamps) and a wide strip; the timm defaults (0.5) and the ImageNet statistics.
+IMAGENET_MEAN = (0.485, 0.456, 0.406)
+IMAGENET_STD = (0.229, 0.224, 0.225)
+PREPROCESS_CASES = [
+    ("landscape 375x500", 375, 500, 224, 0.9, (0.5, 0.5, 0.5), (0.5, 0.5, 0.5), 41),
+    ("square 224", 224, 224, 224, 1.0, IMAGENET_MEAN, IMAGENET_STD, 42),
+    ("portrait 61x37 to 32", 61, 37, 32, 0.875, IMAGENET_MEAN, IMAGENET_STD, 43),
+    ("single pixel to 8", 1, 1, 8, 0.9, (0.5, 0.5, 0.5), (0.5, 0.5, 0.5), 44),
+    ("wide 100x300", 100, 300, 224, 0.95, (0.5, 0.5, 0.5), (0.25, 0.5, 1.0), 45),
+]
+
+
+def preprocess_image(height: int, width: int, seed: int) -> np.ndarray:
+    """Interleaved 8-bit RGB [height, width, 3]."""
+    return np.random.default_rng(seed).integers(0, 256, (height, width, 3), dtype=np.uint8)
+
+
 def vit_images(config: VitConfig, count: int, seed: int) -> np.ndarray:
     rng = np.random.default_rng(seed)
     return rng.standard_normal(count * config.image_elements()).astype(np.float32)
@@ -167,6 +186,15 @@ def main() -> None:
     ref.ref_gelu(x, y, x.size)
     out["gelu/y"] = y
     out["gelu/sha"] = np.array([digest(x)])
+
+    for label, height, width, size, crop, mean, stddev, seed in PREPROCESS_CASES:
+        pixels = preprocess_image(height, width, seed)
+        tensor = oracle.ref_preprocess(pixels, size, crop, mean, stddev)
+        keep = sample_rows(size)
+        out[f"preprocess/{label}/rows"] = keep
+        out[f"preprocess/{label}/y"] = tensor[:, keep, :]
+        out[f"preprocess/{label}/sha"] = np.array(
+            [hashlib.sha256(pixels.tobytes()).hexdigest()])
 
     with tempfile.TemporaryDirectory() as tmp:
         for label, config, weight_seed, std, count, image_seed in VIT_CASES:

@@ -229,3 +229,32 @@ def test_cvw_round_trip_and_rejections():
         path.write_bytes(bytes(versioned))
         with pytest.raises(RuntimeError, match="version 2"):
             cvw.WeightFile.load(path)
+
+
+def test_preprocess_validation_matches_reference():
+    """cuvit_preprocess rejects what cuvit::preprocess rejects (src/runtime/image.cpp:91-99,
+    116-119), with its messages, before touching a device; an empty batch is a no-op."""
+    def call(batch=1, width=8, height=8, size=4, crop=0.9, stddev=(1.0, 1.0, 1.0)):
+        kernels.launch_preprocess(FAKE, FAKE, batch, width, height, size, crop, (0.0, 0.0, 0.0),
+                                  stddev)
+
+    call(batch=0)
+    cases = [(dict(width=0), "Cannot preprocess an empty image"),
+             (dict(height=-1), "Cannot preprocess an empty image"),
+             (dict(size=0), "The preprocessing size must be positive"),
+             (dict(crop=0.0), "The crop fraction must lie in (0, 1]"),
+             (dict(crop=1.01), "The crop fraction must lie in (0, 1]"),
+             (dict(crop=float("nan")), "The crop fraction must lie in (0, 1]"),
+             (dict(stddev=(1.0, 0.0, 1.0)), "A preprocessing standard deviation cannot be zero"),
+             (dict(batch=-1), "The batch cannot be negative")]
+    for kwargs, message in cases:
+        with pytest.raises(InvalidArgument, match=re.escape(message)):
+            call(**kwargs)
+    with pytest.raises(InvalidArgument):
+        kernels.launch_preprocess(FAKE, FAKE, 2, 8, 8, 4, image_stride=8 * 8 * 3 - 1)
+    with pytest.raises(InvalidArgument):
+        kernels.launch_preprocess(None, FAKE, 1, 8, 8, 4)
+    settings = _lib.PreprocessingC()
+    _lib.library().cuvit_preprocessing_default(ctypes.byref(settings))
+    assert settings.size == 224 and abs(settings.crop_fraction - 0.9) < 1e-7
+    assert list(settings.mean) == [0.5] * 3 and list(settings.stddev) == [0.5] * 3

@@ -97,6 +97,26 @@ def test_shard_covers_the_batch_in_order():
         shard(8, 2, 2)
 
 
+def test_c_library_shards_like_the_host_helper():
+    """cuvit_shard -- the partition the C ABI's multi-GPU entry points use (replicas and the
+    NCCL gather's rank order) -- equals the Python helper, and concatenating the parts in
+    index order restores the global image order; bad partitions are rejected."""
+    from cuvit.errors import InvalidArgument
+    from cuvit.replicas import shard, shard_c
+
+    for total in (0, 1, 5, 7, 256, 1024, 1025):
+        for parts in (1, 2, 3, 4, 8):
+            order = []
+            for index in range(parts):
+                first, count = shard_c(total, parts, index)
+                assert (first, count) == shard(total, parts, index)
+                order.extend(range(first, first + count))
+            assert order == list(range(total))
+    for bad in ((5, 0, 0), (5, 2, 2), (5, 2, -1), (-1, 2, 0)):
+        with pytest.raises(InvalidArgument):
+            shard_c(*bad)
+
+
 def test_cpu_lists_and_device_locality_from_sysfs(tmp_path):
     """Each rank binds to its GPU's NUMA-local CPUs (bench.py, N > 1); the topology comes from
     the PCI device's local_cpulist in sysfs, here a fake tree."""

@@ -85,6 +85,27 @@ def test_vit_forward_matches_reference_bitwise(case, golden, oracle_lib):
     np.testing.assert_array_equal(logits, golden[f"vit/{label}/logits"])
 
 
+@pytest.mark.parametrize("case", mg.PREPROCESS_CASES, ids=[c[0] for c in mg.PREPROCESS_CASES])
+def test_preprocess_matches_reference_bitwise(case, golden, oracle_lib):
+    """src/runtime/image.cpp:90-135 -- resize, centre crop, normalise -- bit for bit."""
+    import hashlib
+
+    label, height, width, size, crop, mean, stddev, seed = case
+    pixels = mg.preprocess_image(height, width, seed)
+    assert list(golden[f"preprocess/{label}/sha"]) == [hashlib.sha256(pixels.tobytes()).hexdigest()]
+    got = oracle_lib.preprocess(pixels, size, crop, mean, stddev)
+    rows = golden[f"preprocess/{label}/rows"]
+    np.testing.assert_array_equal(got[:, rows, :], golden[f"preprocess/{label}/y"])
+
+
+def test_preprocess_rejects_what_the_reference_rejects(oracle_lib):
+    pixels = np.zeros((4, 4, 3), np.uint8)
+    for size, crop, stddev in ((0, 0.9, (1, 1, 1)), (8, 0.0, (1, 1, 1)), (8, 1.5, (1, 1, 1)),
+                               (8, 0.9, (1, 0, 1))):
+        with pytest.raises(ValueError):
+            oracle_lib.preprocess(pixels, size, crop, (0, 0, 0), stddev)
+
+
 def test_extract_patches_is_the_documented_gather(oracle_lib):
     # patches[b*P + p][c*pp + r*patch + q] = images[b][c][pr*patch + r][pc*patch + q]
     rng = np.random.default_rng(5)
