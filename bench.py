@@ -65,6 +65,8 @@ def parse_args():
     parser.add_argument("--warmup", type=int, default=5)
     parser.add_argument("--impl", choices=["ours", "reference"], default="ours")
     parser.add_argument("--config", choices=sorted(CONFIGS), default="vit-b")
+    parser.add_argument("--precision", choices=["bf16", "tf32", "fp32"], default=None,
+                        help="override the configuration's precision (profiling runs)")
     parser.add_argument("--profile-passes", type=int, default=5)
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--timeline", action="store_true",
@@ -329,8 +331,10 @@ def measure_single_gemms(torch, device, peak_tf32: float) -> dict:
     through launch_gemm in the FP32-faithful (3xTF32) and TF32 modes. Mean device time per
     launch over 100 launches captured in one CUDA graph (so host call overhead does not
     appear), 5 replays; each launch is one wave or less, so this is a latency figure."""
+    import oracle
     from cuvit import kernels
 
+    ref = oracle.ref_gpu() if oracle.ref_gpu_available() else None
     stream = torch.cuda.current_stream(device)
     rng = np.random.default_rng(0)
     shapes = [("qkv", 197, 576, 192, False, False), ("fc1_gelu", 197, 768, 192, True, False),
@@ -366,6 +370,29 @@ def measure_single_gemms(torch, device, peak_tf32: float) -> dict:
                 "m": m, "n": n, "k": k, "us_per_launch": ms * 1e3,
                 "tflops": flops / (ms * 1e-3) / 1e12,
                 "frac_of_tf32_peak": flops / (ms * 1e-3) / 1e12 / peak_tf32}
+            if math_name == "fp32" and ref is not None:
+                # The reference's own launch_gemm (SIMT FP32, src/kernels/gemm.cu) on the same
+                # operands, captured and timed the same way.
+                def ref_launch():
+                    status = ref.ref_gpu_gemm_async(a.data_ptr(), b.data_ptr(), bias.data_ptr(),
+                                                    c.data_ptr(), m, n, k, 1, 1.0,
+                                                    int(accumulate), int(gelu), side.cuda_stream)
+                    assert status == 0
+
+                with torch.cuda.stream(side):
+                    for _ in range(3):
+                        ref_launch()
+                stream.wait_stream(side)
+                graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(graph, stream=side):
+                    for _ in range(100):
+                        ref_launch()
+                graph.replay()
+                ms_ref = event_ms(torch, stream, graph.replay, 5) / 100
+                del graph
+                results[f"{name}_reference_fp32_gpu"] = {
+                    "m": m, "n": n, "k": k, "us_per_launch": ms_ref * 1e3,
+                    "tflops": flops / (ms_ref * 1e-3) / 1e12}
     kernels.set_math_mode(previous)
     kernels.device_status()
     return results
@@ -397,22 +424,36 @@ def measure_fp32_baselines(torch, device) -> dict:
     cuvit.kernels.device_status()
     ours.close()
     results["ours_fp32_faithful"] = {"images_per_s": batch / (ms * 1e-3), "ms_per_pass": ms}
-    if oracle.ref_gpu_available():
-        ref = oracle.RefGpuModel(config, weights, tensor_specs(config), batch)
+    del images, logits
+    if not oracle.ref_gpu_available():
+        results["reference_fp32_gpu"] = None
+        return results
+    # The reference's FP32 GPU path on every model configuration at its batch (one GPU).
+    results["reference_fp32_gpu"] = {}
+    for name in ("vit-ti", "vit-s", "vit-b", "vit-l"):
+        ref_label, ref_kwargs, ref_batch, _, ref_seed = CONFIGS[name]
+        ref_config = VitConfig(**ref_kwargs)
+        ref_weights = weights if name == "vit-b" else random_weights(ref_config, ref_seed)
+        ref_rng = np.random.default_rng([ref_seed, 0])
+        ref_images = torch.from_numpy(ref_rng.standard_normal(
+            ref_batch * ref_config.image_elements()).astype(np.float32)).to(device)
+        ref_logits = torch.zeros(ref_batch, ref_config.classes, device=device)
+        ref = oracle.RefGpuModel(ref_config, ref_weights, tensor_specs(ref_config), ref_batch)
         handle = stream.cuda_stream
 
         def ref_pass():
-            ref.forward(images.data_ptr(), logits.data_ptr(), batch, handle)
+            ref.forward(ref_images.data_ptr(), ref_logits.data_ptr(), ref_batch, handle)
 
         ref_pass()
         ms_ref = event_ms(torch, stream, ref_pass, 3)
         ref.close()
-        results["reference_fp32_gpu"] = {"images_per_s": batch / (ms_ref * 1e-3),
-                                         "ms_per_pass": ms_ref,
-                                         "kind": "reference (oracle/_ref/libcuvit_ref_gpu.so)"}
-        results["ratio_ours_over_reference"] = ms_ref / ms
-    else:
-        results["reference_fp32_gpu"] = None
+        results["reference_fp32_gpu"][name] = {
+            "workload": f"{ref_label} FP32, batch {ref_batch}",
+            "images_per_s": ref_batch / (ms_ref * 1e-3), "ms_per_pass": ms_ref,
+            "kind": "reference (oracle/_ref/libcuvit_ref_gpu.so)"}
+        if name == "vit-b":
+            results["ratio_ours_over_reference"] = ms_ref / ms
+        del ref_images, ref_logits
     return results
 
 
@@ -422,8 +463,8 @@ def our_arm(args) -> None:
 
     import cuvit
     from cuvit.replicas import Comm, bind_to_gpu_cpus
-    from cuvit.vit import (PRECISION_BF16, PRECISION_TF32, VisionTransformer, VitConfig,
-                           random_weights)
+    from cuvit.vit import (PRECISION_BF16, PRECISION_FP32, PRECISION_TF32, VisionTransformer,
+                           VitConfig, random_weights)
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -438,8 +479,10 @@ def our_arm(args) -> None:
                                 device_id=device)
 
     label, kwargs, batch, precision_name, seed = CONFIGS[args.config]
+    precision_name = args.precision or precision_name
     config = VitConfig(**kwargs)
-    precision = PRECISION_BF16 if precision_name == "bf16" else PRECISION_TF32
+    precision = {"bf16": PRECISION_BF16, "tf32": PRECISION_TF32,
+                 "fp32": PRECISION_FP32}[precision_name]
     weights = random_weights(config, seed)
     model = VisionTransformer(config, weights, max_batch=batch, precision=precision,
                               device=local_rank)
@@ -589,7 +632,7 @@ def our_arm(args) -> None:
             "metric": METRIC, "value": value, "unit": "images/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": elapsed_ms / args.steps, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "bf16" if bf16 else "tf32",
+            "scaling": "weak", "vs_baseline": None, "dtype": precision_name,
             "data": "synthetic N(0,1) images, random-init trunc-normal(0.02) weights",
             "config": {
                 "workload": f"{label} forward, {precision_name.upper()} operands / FP32 "

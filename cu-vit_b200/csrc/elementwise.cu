@@ -351,32 +351,36 @@ __global__ void broadcast_kernel(float* __restrict__ destination,
     }
 }
 
-// tokens[b][t][e] = pos[t][e] + (t == 0 ? cls[e] : 0)
+// tokens[b][t][e] = pos[t][e] + (t == 0 ? cls[e] : 0). Image blockIdx.y; its elements in
+// grid-stride order, so the position index is the element index itself (a 64-bit modulo per
+// element held the old flat form to 0.76 of the write bandwidth).
 __global__ void init_tokens_kernel(float* __restrict__ tokens, const float* __restrict__ cls,
                                    const float* __restrict__ pos, long long per_image,
-                                   int embed, long long total, int vectorised) {
+                                   int embed, int vectorised) {
     dev::timeline_enter();
     dev::grid_dependency_wait();
     dev::grid_launch_dependents();
     const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
-    long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const long long first = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+    float* const image = tokens + static_cast<long long>(blockIdx.y) * per_image;
     if (vectorised) {
-        for (; i < total / 4; i += stride) {
-            const long long within = (i * 4) % per_image;
-            float4 value = reinterpret_cast<const float4*>(pos)[within / 4];
-            if (within < embed) {
-                const float4 c = reinterpret_cast<const float4*>(cls)[within / 4];
+        const float4* const pos4 = reinterpret_cast<const float4*>(pos);
+        const float4* const cls4 = reinterpret_cast<const float4*>(cls);
+        float4* const image4 = reinterpret_cast<float4*>(image);
+        for (long long i = first; i < per_image / 4; i += stride) {
+            float4 value = __ldg(pos4 + i);
+            if (i * 4 < embed) {
+                const float4 c = __ldg(cls4 + i);
                 value.x = c.x + value.x;
                 value.y = c.y + value.y;
                 value.z = c.z + value.z;
                 value.w = c.w + value.w;
             }
-            reinterpret_cast<float4*>(tokens)[i] = value;
+            image4[i] = value;
         }
     } else {
-        for (; i < total; i += stride) {
-            const long long within = i % per_image;
-            tokens[i] = within < embed ? cls[within] + pos[within] : pos[within];
+        for (long long i = first; i < per_image; i += stride) {
+            image[i] = i < embed ? cls[i] + pos[i] : pos[i];
         }
     }
     dev::timeline_exit();
@@ -457,30 +461,61 @@ __global__ void __launch_bounds__(kThreads)
     const int strip = reverse ? static_cast<int>(gridDim.x) - 1 - slot : slot;
     const int image = strip / patch_rows;
     const int pr = strip - image * patch_rows;
-    const int quads = width / 4;                // float4 per image row
-    const int per_channel = patch * quads;      // float4 per channel of the strip
-    const int count = channels * per_channel;   // float4 in the strip
     const int area = patch * patch;
     const long long row_length = static_cast<long long>(channels) * area;
     const In* const base = images + static_cast<long long>(image) * channels * height * width +
                            static_cast<long long>(pr) * patch * width;
     Out* const out = patches + (static_cast<long long>(image) * patch_rows * across +
                                 static_cast<long long>(pr) * across) * row_length;
-    for (int i = threadIdx.x; i < count; i += kThreads) {
-        const int channel = i / per_channel;
-        const int rest = i - channel * per_channel;
-        const int r = rest / quads;
-        const int column = (rest - r * quads) * 4;
-        const int pc = column / patch;
-        const int q = column - pc * patch;
-        const In* const source = base + static_cast<long long>(channel) * height * width +
-                                 static_cast<long long>(r) * width + column;
-        Out* const target = out + pc * row_length + channel * area + r * patch + q;
-        if constexpr (std::is_same_v<In, float>) {
-            store4(target, __ldg(reinterpret_cast<const float4*>(source)));
-        } else {
-            static_assert(std::is_same_v<Out, __nv_bfloat16>, "bfloat16 images give bfloat16");
-            *reinterpret_cast<uint2*>(target) = __ldg(reinterpret_cast<const uint2*>(source));
+    // Thread (x, y): the 4-pixel group x of every image row y, y + blockDim.y, ... of the strip
+    // (channels * patch rows). The group's patch and place in it are fixed per thread, and the
+    // row index advances without division: per-element divisions by the runtime extents held
+    // the one-dimensional form to its issue rate (0.64 of the copy bandwidth).
+    const int quad = static_cast<int>(threadIdx.x);
+    const int column = quad * 4;
+    const int pc = column / patch;
+    const int q = column - pc * patch;
+    const In* const source_column = base + column;
+    Out* const target_column = out + pc * row_length + q;
+    const int rows = channels * patch;
+    const int step = static_cast<int>(blockDim.y); // <= patch (host guarantee)
+    using Vector = std::conditional_t<std::is_same_v<In, float>, float4, uint2>;
+    constexpr int kUnroll = 4; // loads in flight per thread before their stores
+    int channel = 0;
+    int r = static_cast<int>(threadIdx.y);
+    for (int row = static_cast<int>(threadIdx.y); row < rows; row += step * kUnroll) {
+        Vector value[kUnroll];
+        Out* target[kUnroll];
+        int c = channel;
+        int rr = r;
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u) {
+            target[u] = nullptr;
+            if (row + u * step < rows) {
+                value[u] = __ldg(reinterpret_cast<const Vector*>(
+                    source_column + static_cast<long long>(c) * height * width +
+                    static_cast<long long>(rr) * width));
+                target[u] = target_column + c * area + rr * patch;
+            }
+            rr += step;
+            if (rr >= patch) {
+                rr -= patch;
+                ++c;
+            }
+        }
+        channel = c;
+        r = rr;
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u) {
+            if (target[u] != nullptr) {
+                if constexpr (std::is_same_v<In, float>) {
+                    store4(target[u], value[u]);
+                } else {
+                    static_assert(std::is_same_v<Out, __nv_bfloat16>,
+                                  "bfloat16 images give bfloat16");
+                    *reinterpret_cast<uint2*>(target[u]) = value[u];
+                }
+            }
         }
     }
     dev::timeline_exit();
@@ -655,6 +690,16 @@ int softmax_impl(const float* input, float* output, int rows, int columns, long 
     return host::after_launch("softmax");
 }
 
+// Block of the strip kernel: one thread per 4-pixel group of an image row (x) and as many rows
+// at once as fit about 256 threads (y), at most one patch of rows.
+constexpr int kMaxStripQuads = 1024;
+dim3 strip_block(int width, int patch) {
+    const int quads = width / 4;
+    int y = kThreads / quads;
+    y = y < 1 ? 1 : (y > patch ? patch : y);
+    return dim3(static_cast<unsigned>(quads), static_cast<unsigned>(y));
+}
+
 int extract_patches_impl(const float* images, void* patches, int out_dtype, int batch,
                          int channels, int height, int width, int patch, cudaStream_t stream) {
     if (batch == 0) {
@@ -686,13 +731,14 @@ int extract_patches_impl(const float* images, void* patches, int out_dtype, int 
                      aligned(patches, bf16 ? 8 : 16);
     const unsigned blocks = static_cast<unsigned>(grid);
     const long long strips = static_cast<long long>(batch) * (height / patch);
-    const bool by_rows = vec && strips <= 0x7FFFFFFFLL;
+    const bool by_rows = vec && strips <= 0x7FFFFFFFLL && width / 4 <= kMaxStripQuads;
     const auto run = [&](auto* out) {
         using Out = std::remove_pointer_t<decltype(out)>;
         if (by_rows) {
             host::pdl_launch(extract_patch_rows_kernel<float, Out>, static_cast<unsigned>(strips),
-                             kThreads, 0, stream, images, out, channels, height, width, patch,
-                             across, height / patch, host::reverse_sweep() ? 1 : 0);
+                             strip_block(width, patch), 0, stream, images, out, channels, height,
+                             width, patch, across, height / patch,
+                             host::reverse_sweep() ? 1 : 0);
         } else if (vec) {
             host::pdl_launch(extract_patches_kernel<Out, 4>, blocks, kThreads, 0, stream,
                              images, out, channels, height, width, patch, across, per_image,
@@ -717,7 +763,7 @@ int extract_patches_impl(const float* images, void* patches, int out_dtype, int 
 
 bool bf16_patch_gather_supported(int height, int width, int patch) {
     return patch > 0 && patch % 4 == 0 && width % 4 == 0 && height % patch == 0 &&
-           width % patch == 0;
+           width % patch == 0 && width / 4 <= kMaxStripQuads;
 }
 
 int extract_patches_bf16(const __nv_bfloat16* images, __nv_bfloat16* patches, int batch,
@@ -736,7 +782,8 @@ int extract_patches_bf16(const __nv_bfloat16* images, __nv_bfloat16* patches, in
         return host::fail(CUVIT_LENGTH_ERROR, "Elementwise launch exceeds the CUDA grid limit");
     }
     host::pdl_launch(extract_patch_rows_kernel<__nv_bfloat16, __nv_bfloat16>,
-                     static_cast<unsigned>(strips), kThreads, 0, stream, images, patches,
+                     static_cast<unsigned>(strips), strip_block(width, patch), 0, stream, images,
+                     patches,
                      channels, height, width, patch, width / patch, height / patch,
                      host::reverse_sweep() ? 1 : 0);
     return host::after_launch("extract_patches");
@@ -886,18 +933,22 @@ int cuvit_init_tokens(float* tokens, const float* class_token, const float* posi
         return fail(CUVIT_INVALID_ARGUMENT, "token initialisation operands cannot be null");
     }
     const long long per_image = static_cast<long long>(tokens_per_image) * embed;
-    const long long total = per_image * batch;
-    const long long grid = elementwise_grid(total);
-    if (grid < 0) {
+    if (elementwise_grid(per_image * batch) < 0 || batch > 65535) {
         return fail(CUVIT_LENGTH_ERROR, "Elementwise launch exceeds the CUDA grid limit");
     }
     const int vec = embed % 4 == 0 && aligned(tokens, 16) && aligned(class_token, 16) &&
                             aligned(position, 16)
                         ? 1
                         : 0;
-    cuvit::host::pdl_launch(init_tokens_kernel, static_cast<unsigned>(grid), kThreads, 0,
+    // About 16 blocks per SM in all, spread over the images (each image's row blockIdx.y).
+    const long long items = vec ? per_image / 4 : per_image;
+    long long across = (items + kThreads - 1) / kThreads;
+    const long long share = (148LL * 16 + batch - 1) / batch;
+    across = across < share ? across : share;
+    const dim3 grid(static_cast<unsigned>(across < 1 ? 1 : across), static_cast<unsigned>(batch));
+    cuvit::host::pdl_launch(init_tokens_kernel, grid, kThreads, 0,
                             reinterpret_cast<cudaStream_t>(stream), tokens, class_token, position,
-                            per_image, embed, total, vec);
+                            per_image, embed, vec);
     return cuvit::host::after_launch("init_tokens");
 }
 

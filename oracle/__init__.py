@@ -269,6 +269,9 @@ def ref_gpu() -> ctypes.CDLL:
     library = _load(REF_GPU_LIB, "ref_gpu")
     library.ref_gpu_gemm.argtypes = [ctypes.c_void_p] * 4 + [_i, _i, _i, _i, _f, _i, _i]
     library.ref_gpu_gemm.restype = _i
+    library.ref_gpu_gemm_async.argtypes = [ctypes.c_void_p] * 4 + [_i, _i, _i, _i, _f, _i, _i,
+                                                                  ctypes.c_void_p]
+    library.ref_gpu_gemm_async.restype = _i
     library.ref_gpu_vit_create.argtypes = [ctypes.c_char_p, ctypes.c_void_p, _f, _i]
     library.ref_gpu_vit_create.restype = ctypes.c_void_p
     library.ref_gpu_vit_forward.argtypes = [ctypes.c_void_p] * 3 + [_i, ctypes.c_void_p]

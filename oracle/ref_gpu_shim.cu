@@ -26,6 +26,24 @@ REF_API int ref_gpu_gemm(const float* a, const float* b, const float* bias, floa
     }
 }
 
+// The same launch without the synchronisation, on `stream` (so a caller can time it with
+// events or capture it in a CUDA graph). Returns 0, or -1 when the reference throws.
+REF_API int ref_gpu_gemm_async(const float* a, const float* b, const float* bias, float* c,
+                               int m, int n, int k, int transposed, float alpha, int accumulate,
+                               int gelu, void* stream) {
+    try {
+        cuvit::GemmProblem problem = cuvit::gemm_problem(
+            m, n, k, transposed ? cuvit::GemmLayout::kTransposed : cuvit::GemmLayout::kNoTranspose);
+        problem.alpha = alpha;
+        problem.epilogue.accumulate = accumulate != 0;
+        problem.epilogue.gelu = gelu != 0;
+        cuvit::launch_gemm(a, b, bias, c, problem, static_cast<cudaStream_t>(stream));
+        return 0;
+    } catch (const std::exception&) {
+        return -1;
+    }
+}
+
 REF_API void* ref_gpu_vit_create(const char* weights_path, const int* c, float epsilon,
                                  int max_batch) {
     try {

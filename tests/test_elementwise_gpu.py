@@ -126,8 +126,14 @@ def test_softmax_row_stride(cuda):
     np.testing.assert_array_equal(got[:, columns:], x.reshape(rows, stride)[:, columns:])
 
 
+# The strip kernel's block shapes (row groups of 4, 2, 16 and 1, a patch of 4 rows capping
+# them, and a width past its 1024-group limit, which takes the per-element kernel) and the
+# unaligned fallbacks.
 @pytest.mark.parametrize("batch,channels,size,patch", [(2, 3, 224, 16), (3, 3, 32, 8),
-                                                       (1, 1, 12, 3), (4, 2, 10, 5)])
+                                                       (1, 1, 12, 3), (4, 2, 10, 5),
+                                                       (2, 3, 384, 16), (1, 3, 64, 32),
+                                                       (2, 4, 48, 4), (1, 3, 1024, 16),
+                                                       (1, 1, 4112, 16)])
 def test_extract_patches_is_bit_exact(batch, channels, size, patch, cuda):
     images = np.random.default_rng(size).standard_normal(
         batch * channels * size * size).astype(np.float32)
