@@ -598,27 +598,58 @@ __global__ void __launch_bounds__(TcShape<ElemBytes, BN, Split>::kThreads, 1)
             if (!dev::mbar_wait(full_bar(stage), phase, p.status)) {
                 break;
             }
-            float4* const hi = reinterpret_cast<float4*>(smem + (stage_a(stage) - base));
-            float4* const lo = reinterpret_cast<float4*>(smem + (stage_a(stage) - base) +
-                                                         Shape::kABytes + Shape::kBBytes);
+            // In place: hi = rn_tf32(x) over the landed stage, lo = rn_tf32(x - hi) into the
+            // stage's second half. Each thread loads four vectors before converting them, with
+            // the rounding done by integer adds and masks, which is exact for |x| < 2^127 (no
+            // carry can reach the exponent, and x - hi is exact in FP32); a warp that meets a
+            // larger value, an infinity or a NaN redoes its vectors with the checked rounding.
+            // Rounding the remainder (rather than letting the MMA truncate it) leaves at most
+            // 2^-22 |x| of error per operand.
+            const uint32_t hi_addr = stage_a(stage);
+            const uint32_t lo_addr = stage_a(stage) + Shape::kABytes + Shape::kBBytes;
             constexpr int kVectors = (Shape::kABytes + Shape::kBBytes) / 16;
-#pragma unroll 4
-            for (int i = t; i < kVectors; i += 128) {
-                const float4 x = hi[i];
-                float4 h;
-                h.x = dev::round_to_tf32(x.x);
-                h.y = dev::round_to_tf32(x.y);
-                h.z = dev::round_to_tf32(x.z);
-                h.w = dev::round_to_tf32(x.w);
-                // x - h is exact in FP32; rounding it (rather than letting the MMA truncate)
-                // leaves at most 2^-22 |x| of error per operand.
-                float4 l;
-                l.x = isfinite(x.x) ? dev::round_to_tf32(x.x - h.x) : 0.0F;
-                l.y = isfinite(x.y) ? dev::round_to_tf32(x.y - h.y) : 0.0F;
-                l.z = isfinite(x.z) ? dev::round_to_tf32(x.z - h.z) : 0.0F;
-                l.w = isfinite(x.w) ? dev::round_to_tf32(x.w - h.w) : 0.0F;
-                hi[i] = h;
-                lo[i] = l;
+            static_assert(kVectors % 512 == 0, "whole rounds of four vectors per thread");
+#pragma unroll 1
+            for (int first = t; first < kVectors; first += 512) {
+                float x[4][4];
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    dev::ld_shared_v4(hi_addr + 16u * static_cast<uint32_t>(first + 128 * u),
+                                      x[u]);
+                }
+                float h[4][4];
+                float l[4][4];
+                bool special = false;
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const uint32_t bits = __float_as_uint(x[u][j]);
+                        special |= (bits & 0x7FFFFFFFu) >= 0x7F000000u;
+                        h[u][j] = __uint_as_float((bits + 0x1000u) & 0xFFFFE000u);
+                        l[u][j] = __uint_as_float(
+                            (__float_as_uint(x[u][j] - h[u][j]) + 0x1000u) & 0xFFFFE000u);
+                    }
+                }
+                if (__any_sync(0xFFFFFFFFu, special)) {
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) {
+                            h[u][j] = dev::round_to_tf32(x[u][j]);
+                            const float rest = dev::round_to_tf32(x[u][j] - h[u][j]);
+                            l[u][j] = (__float_as_uint(x[u][j]) & 0x7F800000u) == 0x7F800000u
+                                          ? 0.0F
+                                          : rest;
+                        }
+                    }
+                }
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const uint32_t offset = 16u * static_cast<uint32_t>(first + 128 * u);
+                    dev::st_shared_v4(hi_addr + offset, h[u]);
+                    dev::st_shared_v4(lo_addr + offset, l[u]);
+                }
             }
             dev::fence_proxy_async_shared();
             dev::mbar_arrive(conv_bar(stage));

@@ -169,6 +169,19 @@ __device__ __forceinline__ void named_barrier_sync(uint32_t id, uint32_t threads
 }
 
 // Makes generic-proxy shared-memory writes visible to the async proxy (TMA, tensor core).
+// Four floats from / to a 16-byte aligned shared-memory address.
+__device__ __forceinline__ void ld_shared_v4(uint32_t address, float (&v)[4]) {
+    asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v[0]), "=f"(v[1]), "=f"(v[2]), "=f"(v[3])
+                 : "r"(address));
+}
+
+__device__ __forceinline__ void st_shared_v4(uint32_t address, const float (&v)[4]) {
+    asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(address), "f"(v[0]),
+                 "f"(v[1]), "f"(v[2]), "f"(v[3])
+                 : "memory");
+}
+
 __device__ __forceinline__ void fence_proxy_async_shared() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
@@ -478,17 +491,15 @@ __device__ __forceinline__ float gelu_erf(float value) {
 // Rounds an FP32 value to the nearest TF32 value (10-bit mantissa, ties away from zero in
 // magnitude); non-finite values pass through. The tensor core would otherwise truncate the
 // low 13 mantissa bits of a TF32 operand, a bias that accumulates over long reductions.
+// Written with selects rather than branches: in the 3xTF32 splitter's loop the branches kept
+// its shared-memory loads from overlapping and made the conversion six times slower.
 __device__ __forceinline__ float round_to_tf32(float x) {
     const uint32_t bits = __float_as_uint(x);
-    if ((bits & 0x7F800000u) == 0x7F800000u) {
-        return x;
-    }
     const uint32_t rounded = (bits + 0x1000u) & 0xFFFFE000u;
-    // A carry into an all-ones exponent would turn a finite value into infinity.
-    if ((rounded & 0x7F800000u) == 0x7F800000u) {
-        return __uint_as_float(bits & 0xFFFFE000u);
-    }
-    return __uint_as_float(rounded);
+    // A carry into an all-ones exponent would turn a finite value into infinity: truncate.
+    const uint32_t finite_result =
+        (rounded & 0x7F800000u) == 0x7F800000u ? (bits & 0xFFFFE000u) : rounded;
+    return __uint_as_float((bits & 0x7F800000u) == 0x7F800000u ? bits : finite_result);
 }
 
 __device__ __forceinline__ float ex2_approx(float x) {

@@ -215,6 +215,33 @@ def test_gelu_epilogue_with_bf16_output(cuda):
     np.testing.assert_allclose(got, bf16_round(got32), rtol=2 ** -7, atol=1e-6)
 
 
+@pytest.mark.parametrize("layout", [N_LAYOUT, T], ids=["kN", "kT"])
+def test_fp32_split_handles_huge_and_non_finite_operands(layout, cuda):
+    """The 3xTF32 splitter rounds with integer adds, exact below 2^127; operands at or above
+    it and infinities / NaNs take its checked rounding. Huge finite operands stay within the
+    reference tolerance; a row with an infinity or a NaN gives non-finite results exactly
+    where the FP32 oracle does, and every other output is unaffected."""
+    m, n, k = 160, 136, 96
+    rng = np.random.default_rng(29)
+    a = rng.uniform(-1, 1, m * k).astype(np.float32)
+    b = (1e-3 * rng.uniform(-1, 1, k * n)).astype(np.float32)
+    a[5 * k + 3] = 3.0e38         # exponent 254
+    a[7 * k + 90] = -2.9e38
+    a[9 * k + 11] = 1.7014e38     # exactly 2^127-ish
+    a[20 * k + 4] = np.inf
+    a[30 * k + 40] = np.nan
+    transposed = layout == T
+    want = oracle.gemm(a, b, None, np.zeros(m * n, np.float32), m, n, k, transposed)
+    got = run(a, b, None, np.full(m * n, np.nan, np.float32), gemm_problem(m, n, k, layout),
+              kernels.MATH_FP32, cuda)
+    np.testing.assert_array_equal(np.isfinite(got), np.isfinite(want))
+    finite = np.isfinite(want)
+    with np.errstate(invalid="ignore", over="ignore"):
+        scale = oracle.gemm_term_magnitudes(np.nan_to_num(a, posinf=0.0), b, m, n, k, transposed)
+    assert_close_scaled(got[finite], want[finite], scale[finite], FP32_RTOL, 1e-6,
+                        f"huge operands layout {layout}")
+
+
 def test_zero_k_produces_the_bias_exactly(cuda):
     m, n = 8, 8
     bias = np.random.default_rng(5).standard_normal(n).astype(np.float32)
