@@ -79,3 +79,32 @@ def test_fused_attention_is_deterministic_and_batch_invariant(cuda):
     for b in range(batch):
         alone = run_attention(per_image[b], 1, tokens, heads, kernels.DTYPE_BF16, cuda)
         np.testing.assert_array_equal(alone[0], first[b])
+
+
+@pytest.mark.parametrize("late_block,boost", [(2, 12.0), (3, 9.0), (1, 14.0), (2, 4.0)])
+def test_fused_attention_row_maximum_in_a_later_key_block(late_block, boost, cuda):
+    """Rows whose maximum sits in one narrow group of keys far from the first ones: a few keys
+    of the 64-key block `late_block` score `boost` (natural-log units) above all others, so
+    the exponentials span up to 2^20, and each row's maximum lies in the part of the keys the
+    second softmax warpgroup (or the first, for block 1) reads; against the oracle's exact
+    softmax."""
+    batch, tokens, heads = 2, 197, 2
+    e = heads * 64
+    rng = np.random.default_rng(int(boost * 10) + late_block)
+    qkv = 0.3 * rng.standard_normal((batch, tokens, 3, e)).astype(np.float32)
+    direction = rng.standard_normal(64).astype(np.float32)
+    direction /= np.linalg.norm(direction)
+    first = late_block * 64 + 3
+    keys = slice(first, min(first + 5, tokens))
+    for h in range(heads):
+        cols = slice(h * 64, (h + 1) * 64)
+        qkv[:, :, 0, cols] = 4.0 * direction          # every query along `direction`
+        # s = 4 * a for these keys: 0.125 * s = boost  ->  a = 2 * boost
+        qkv[:, keys, 1, cols] = (2.0 * boost) * direction
+    qkv = bf16_round(qkv.reshape(-1))
+    got = run_attention(qkv, batch, tokens, heads, kernels.DTYPE_BF16, cuda)
+    want = expected(qkv, batch, tokens, heads)
+    assert np.isfinite(got).all()
+    v_max = np.abs(qkv.reshape(batch, tokens, 3, e)[:, :, 2]).max()
+    err = np.abs(got - want).max()
+    assert err <= 1e-2 * v_max, f"max error {err:.3g} vs bound {1e-2 * v_max:.3g}"
