@@ -258,3 +258,25 @@ def test_preprocess_validation_matches_reference():
     _lib.library().cuvit_preprocessing_default(ctypes.byref(settings))
     assert settings.size == 224 and abs(settings.crop_fraction - 0.9) < 1e-7
     assert list(settings.mean) == [0.5] * 3 and list(settings.stddev) == [0.5] * 3
+
+
+def test_multi_gpu_entry_points_validate_on_the_host():
+    """The communicator's id comes from NCCL without a GPU; bad ranks, worlds and buffers are
+    rejected before NCCL or a device is touched."""
+    from cuvit.replicas import Comm
+
+    first, second = Comm.unique_id(), Comm.unique_id()
+    assert len(first) == 128 and first != second
+    lib = cuvit.library()
+    handle = ctypes.c_void_p(0)
+    buffer = ctypes.create_string_buffer(first, 128)
+    for world, rank, device in ((0, 0, 0), (2, 2, 0), (2, -1, 0), (1, 0, -1)):
+        assert lib.cuvit_comm_create(buffer, world, rank, device,
+                                     ctypes.byref(handle)) == _lib.INVALID_ARGUMENT
+        assert not handle.value
+    assert lib.cuvit_comm_unique_id(buffer, 64) == _lib.INVALID_ARGUMENT
+    assert lib.cuvit_gather_logits(None, FAKE, FAKE, 4, 10, 0, None) == _lib.INVALID_ARGUMENT
+    assert lib.cuvit_comm_destroy(None) == _lib.OK
+    assert lib.cuvit_replicas_destroy(None) == _lib.OK
+    assert lib.cuvit_replicas_device_count(None) == 0
+    assert lib.cuvit_replicas_forward_host(None, FAKE, FAKE, 1) == _lib.INVALID_ARGUMENT
