@@ -2,8 +2,9 @@
  * cuvit_b200.h -- C ABI of the B200 (sm_100a) implementation of Cu-Vit's hot path.
  *
  * Every entry point takes plain device pointers, sizes and a CUDA stream, returns a
- * cuvit_status, and allocates nothing on the calling path (the model runner allocates its
- * arenas once, at creation, like the reference's VisionTransformer constructor). Argument
+ * cuvit_status, and allocates nothing on the calling path (the model runner, the replicas and
+ * the communicator allocate once, at creation, like the reference's VisionTransformer
+ * constructor; the instrumented build's timeline table is allocated by its first reset). Argument
  * validation happens on the host before any launch, in the same order and with the same
  * outcome classes as the reference's C++ launchers:
  *
