@@ -398,6 +398,47 @@ def measure_single_gemms(torch, device, peak_tf32: float) -> dict:
     return results
 
 
+def measure_preprocess(torch, device) -> dict:
+    """Image preprocessing (the input pipeline): 256 interleaved 8-bit RGB images of 500 x 375
+    pixels to the ViT-B input tensor (resize of the shorter side to 248, centre crop 224,
+    normalisation) by cuvit_preprocess on the device, 20 launches timed with CUDA events,
+    against the reference's host preprocess (src/runtime/image.cpp:90-135, compiled into
+    oracle/_ref) on one image per host thread over a sample of 2 x threads images."""
+    import concurrent.futures
+
+    import oracle
+    from cuvit import kernels
+
+    batch, height, width, size = 256, 375, 500, 224
+    rng = np.random.default_rng(17)
+    pixels = rng.integers(0, 256, (batch, height, width, 3), dtype=np.uint8)
+    d_pixels = torch.from_numpy(pixels.reshape(batch, -1)).to(device)
+    out = torch.empty((batch, 3, size, size), device=device)
+    stream = torch.cuda.current_stream(device)
+
+    def launch():
+        kernels.launch_preprocess(d_pixels, out, batch, width, height, size, 0.9, stream=stream)
+
+    for _ in range(3):
+        launch()
+    ms = event_ms(torch, stream, launch, 20)
+    kernels.device_status()
+    moved = pixels.nbytes + out.numel() * 4
+    result = {"workload": f"{batch} RGB images {width}x{height} -> 3x{size}x{size} FP32",
+              "us_per_batch": ms * 1e3, "images_per_s": batch / (ms * 1e-3),
+              "gbs": moved / (ms * 1e-3) / 1e9}
+    if oracle.ref_cpu_available():
+        threads = os.cpu_count() or 1
+        sample = pixels[: min(batch, 2 * threads)]
+        start = time.perf_counter()
+        with concurrent.futures.ThreadPoolExecutor(threads) as pool:
+            list(pool.map(lambda p: oracle.ref_preprocess(p, size, 0.9), sample))
+        seconds = time.perf_counter() - start
+        result["reference_host"] = {"images_per_s": len(sample) / seconds, "threads": threads,
+                                    "kind": "reference (oracle/_ref, cuvit::preprocess)"}
+    return result
+
+
 def measure_fp32_baselines(torch, device) -> dict:
     """ViT-B/16 at batch 256 in FP32 on one GPU: the reference's own FP32 GPU path
     (src/model/vit.cu built for sm_100a into oracle/_ref; a second baseline, never the
@@ -621,6 +662,7 @@ def our_arm(args) -> None:
             torch, device, peak.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]), peak_tf32)
         extras["single_gemms"] = measure_single_gemms(torch, device, peak_tf32)
         extras["fp32_baselines"] = measure_fp32_baselines(torch, device)
+        extras["preprocess"] = measure_preprocess(torch, device)
 
     total_images = world * batch * args.steps
     value = total_images / (elapsed_ms * 1e-3)
