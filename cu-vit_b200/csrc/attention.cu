@@ -192,7 +192,7 @@ __global__ void __launch_bounds__(kThreads)
         const uint32_t lane_field = static_cast<uint32_t>(quarter * 32) << 16;
         const int chunks = (p.n_keys + 31) / 32;
         for (int t = 0; t < p.q_tiles; ++t) {
-            if (!dev::mbar_wait(bar_s, t & 1, p.status)) {
+            if (!dev::mbar_wait_warp(bar_s, t & 1, p.status)) {
                 break;
             }
             dev::tc_fence_after();
@@ -252,7 +252,7 @@ __global__ void __launch_bounds__(kThreads)
             dev::tmem_wait_store();
             dev::tc_fence_before();
             dev::mbar_arrive(bar_p);
-            if (!dev::mbar_wait(bar_o, t & 1, p.status)) {
+            if (!dev::mbar_wait_warp(bar_o, t & 1, p.status)) {
                 break;
             }
             dev::tc_fence_after();
@@ -547,7 +547,7 @@ __global__ void __launch_bounds__(kPipeThreads, 1)
             int i = 0;
             for (int pair = blockIdx.x; pair < p.pairs; pair += gridDim.x, ++i) {
                 const uint32_t parity = static_cast<uint32_t>(i & 1);
-                if (!dev::mbar_wait(bar(kSFull, t), parity, p.status)) {
+                if (!dev::mbar_wait_warp(bar(kSFull, t), parity, p.status)) {
                     break;
                 }
                 dev::tc_fence_after();
@@ -669,7 +669,7 @@ __global__ void __launch_bounds__(kPipeThreads, 1)
                 }
                 dev::tc_fence_before();
                 dev::mbar_arrive(bar(kPFull, t));
-                if (!dev::mbar_wait(bar(kOFull, t), parity, p.status)) {
+                if (!dev::mbar_wait_warp(bar(kOFull, t), parity, p.status)) {
                     break;
                 }
                 dev::tc_fence_after();

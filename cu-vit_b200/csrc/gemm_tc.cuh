@@ -538,7 +538,7 @@ __global__ void __launch_bounds__(TcShape<ElemBytes, BN, Split>::kThreads, 1)
             batch_coords(entry, p.inner, index, outer);
             const int acc = local & 1;
             const uint32_t acc_phase = (local >> 1) & 1;
-            if (!dev::mbar_wait(tfull_bar(acc), acc_phase, p.status)) {
+            if (!dev::mbar_wait_warp(tfull_bar(acc), acc_phase, p.status)) {
                 break;
             }
             dev::tc_fence_after();
@@ -595,7 +595,7 @@ __global__ void __launch_bounds__(TcShape<ElemBytes, BN, Split>::kThreads, 1)
              static_cast<int>(gridDim.x)) *
             p.k_blocks;
         for (int step = 0; step < total_blocks; ++step) {
-            if (!dev::mbar_wait(full_bar(stage), phase, p.status)) {
+            if (!dev::mbar_wait_warp(full_bar(stage), phase, p.status)) {
                 break;
             }
             // In place: hi = rn_tf32(x) over the landed stage, lo = rn_tf32(x - hi) into the

@@ -253,7 +253,7 @@ __global__ void __launch_bounds__(PairShape<BN>::kThreads, 1)
             batch_coords(entry, p.inner, index, outer);
             const int acc = local & 1;
             const uint32_t acc_phase = (local >> 1) & 1;
-            if (!dev::mbar_wait(tfull_bar(acc), acc_phase, p.status)) {
+            if (!dev::mbar_wait_warp(tfull_bar(acc), acc_phase, p.status)) {
                 break;
             }
             dev::tc_fence_after();

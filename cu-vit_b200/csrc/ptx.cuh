@@ -93,6 +93,13 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, unsigne
     }
 }
 
+// mbar_wait by all 32 lanes of a warp, succeeding or failing for the whole warp, so that a
+// warp-wide instruction after it (tcgen05.ld / st are .sync.aligned) never runs with some lanes
+// gone: lanes of one warp can disagree when the wait runs out.
+__device__ __forceinline__ bool mbar_wait_warp(uint32_t bar, uint32_t parity, unsigned* status) {
+    return __all_sync(0xFFFFFFFFu, mbar_wait(bar, parity, status));
+}
+
 // Waits up to limit_ns for a phase regardless of the status word: used after a failure to
 // let this thread's own copies in flight land before the CTA exits.
 __device__ __forceinline__ bool mbar_drain_wait(uint32_t bar, uint32_t parity,

@@ -181,4 +181,16 @@ inline void launch_attention(const void* qkv, void* context, int dtype, int batc
                                      detail::stream_of(stream)));
 }
 
+// Device counterpart of cuvit::preprocess (include/cuvit/image.hpp of the reference, a host
+// function there): `batch` interleaved 8-bit RGB images of width x height on the device,
+// image_stride bytes apart (0 = packed), to the planar [batch, 3, size, size] model input,
+// bit-identical to the reference's host result. Throws std::invalid_argument where the
+// reference does (empty image, size <= 0, crop fraction outside (0, 1], zero deviation).
+inline void launch_preprocess(const std::uint8_t* pixels, int batch, int width, int height,
+                              const cuvit_preprocessing& settings, float* tensor,
+                              std::int64_t image_stride = 0, cudaStream_t stream = nullptr) {
+    detail::raise_on(cuvit_preprocess(pixels, batch, width, height, image_stride, &settings,
+                                      tensor, detail::stream_of(stream)));
+}
+
 } // namespace cuvit
