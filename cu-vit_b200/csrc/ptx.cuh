@@ -175,7 +175,6 @@ __device__ __forceinline__ void named_barrier_sync(uint32_t id, uint32_t threads
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
-// Makes generic-proxy shared-memory writes visible to the async proxy (TMA, tensor core).
 // Four floats from / to a 16-byte aligned shared-memory address.
 __device__ __forceinline__ void ld_shared_v4(uint32_t address, float (&v)[4]) {
     asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
@@ -189,6 +188,7 @@ __device__ __forceinline__ void st_shared_v4(uint32_t address, const float (&v)[
                  : "memory");
 }
 
+// Makes generic-proxy shared-memory writes visible to the async proxy (TMA, tensor core).
 __device__ __forceinline__ void fence_proxy_async_shared() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }

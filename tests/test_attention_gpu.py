@@ -53,6 +53,23 @@ def test_fused_attention_matches_reference_attention(dtype, batch, tokens, heads
     assert err <= 1e-2 * v_max, f"max error {err:.3g} vs bound {1e-2 * v_max:.3g}"
 
 
+@pytest.mark.parametrize("batch,tokens,heads", [(26, 197, 12), (50, 80, 8), (40, 128, 8),
+                                                (60, 129, 5), (2, 224, 100)])
+def test_fused_attention_several_pairs_per_cta(batch, tokens, heads, cuda):
+    """More (image, head) pairs than SMs, so each persistent CTA walks two or three pairs and
+    reuses its shared-memory and tensor-memory buffers; shapes with one query tile (every TMEM
+    lane quarter idle past 80 tokens), two tiles, a one-row second tile, and 224 tokens (the
+    widest score buffer)."""
+    rng = np.random.default_rng(batch * 7 + tokens + heads)
+    qkv = bf16_round(rng.standard_normal(batch * tokens * 3 * heads * 64).astype(np.float32))
+    got = run_attention(qkv, batch, tokens, heads, kernels.DTYPE_BF16, cuda)
+    want = expected(qkv, batch, tokens, heads)
+    assert np.isfinite(got).all()
+    v_max = np.abs(qkv.reshape(batch, tokens, 3, heads * 64)[:, :, 2]).max()
+    err = np.abs(got - want).max()
+    assert err <= 1e-2 * v_max, f"max error {err:.3g} vs bound {1e-2 * v_max:.3g}"
+
+
 def test_fused_attention_sharp_and_flat_rows(cuda):
     """Large logits (near one-hot softmax) and all-equal keys (uniform softmax)."""
     batch, tokens, heads = 1, 197, 2
