@@ -55,6 +55,9 @@ CONFIGS = {
               "bf16", 4),
 }
 
+# Measurements beside the headline on one GPU (all by default).
+EXTRAS = ("configs", "single_gemms", "fp32_baselines", "preprocess")
+
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
 
@@ -73,6 +76,8 @@ def parse_args():
                         help="device timeline of one graph-replayed pass (instrumented build)")
     parser.add_argument("--no-extras", action="store_true",
                         help="skip the other configurations, single GEMMs and FP32 baselines")
+    parser.add_argument("--extra", action="append", choices=EXTRAS, default=None,
+                        help="run only the named extra measurements (repeatable; profiling runs)")
     return parser.parse_args()
 
 
@@ -655,14 +660,22 @@ def our_arm(args) -> None:
     # FP32 comparison with the reference's own GPU path, each timed in this run beside the
     # headline (which they do not touch).
     extras = {}
-    if world == 1 and not args.no_extras:
-        peak_tf32 = measure_tf32_peak(torch, device)
-        extras["tf32_peak_tflops"] = peak_tf32
-        extras["configs"] = measure_other_configs(
-            torch, device, peak.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]), peak_tf32)
-        extras["single_gemms"] = measure_single_gemms(torch, device, peak_tf32)
-        extras["fp32_baselines"] = measure_fp32_baselines(torch, device)
-        extras["preprocess"] = measure_preprocess(torch, device)
+    wanted = set() if args.no_extras else set(args.extra or EXTRAS)
+    if world == 1 and wanted:
+        peak_tf32 = None
+        if wanted & {"configs", "single_gemms"}:
+            peak_tf32 = measure_tf32_peak(torch, device)
+            extras["tf32_peak_tflops"] = peak_tf32
+        if "configs" in wanted:
+            extras["configs"] = measure_other_configs(
+                torch, device, peak.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]),
+                peak_tf32)
+        if "single_gemms" in wanted:
+            extras["single_gemms"] = measure_single_gemms(torch, device, peak_tf32)
+        if "fp32_baselines" in wanted:
+            extras["fp32_baselines"] = measure_fp32_baselines(torch, device)
+        if "preprocess" in wanted:
+            extras["preprocess"] = measure_preprocess(torch, device)
 
     total_images = world * batch * args.steps
     value = total_images / (elapsed_ms * 1e-3)

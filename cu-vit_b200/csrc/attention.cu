@@ -22,7 +22,6 @@
 #include <cuda_bf16.h>
 
 #include <cstdint>
-#include <mutex>
 
 namespace cuvit::attn {
 namespace {
@@ -833,13 +832,7 @@ int launch_bf16_pipelined(const void* qkv, void* context, int batch, int tokens,
 
     const int smem = pipe_smem_bytes(buffer_bytes);
     auto* kernel = &attention_bf16_pipelined;
-    static std::once_flag once;
-    static cudaError_t attribute_error = cudaSuccess;
-    std::call_once(once, [kernel]() {
-        attribute_error = cudaFuncSetAttribute(
-            kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-    });
-    CUVIT_TRY_CUDA(attribute_error);
+    CUVIT_TRY_CUDA(host::allow_dynamic_smem(reinterpret_cast<const void*>(kernel), 227 * 1024));
     const int grid = params.pairs < device.sm_count ? params.pairs : device.sm_count;
     host::pdl_launch(kernel, grid, kPipeThreads, smem, stream, map_q, map_kv, map_ctx, params);
     return host::after_launch("attention_bf16_pipelined");
@@ -897,13 +890,7 @@ int launch_typed(const void* qkv, void* context, int batch, int tokens, int head
         smem = L::kMinSmem;
     }
     auto* kernel = &attention_kernel<ElemBytes>;
-    static std::once_flag once;
-    static cudaError_t attribute_error = cudaSuccess;
-    std::call_once(once, [kernel]() {
-        attribute_error = cudaFuncSetAttribute(
-            kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-    });
-    CUVIT_TRY_CUDA(attribute_error);
+    CUVIT_TRY_CUDA(host::allow_dynamic_smem(reinterpret_cast<const void*>(kernel), 227 * 1024));
     host::pdl_launch(kernel, batch * heads, kThreads, smem, stream, map_q, map_kv, map_v,
                      params);
     return host::after_launch("attention_kernel");

@@ -6,7 +6,6 @@
 
 #include <cstdlib>
 #include <cstring>
-#include <mutex>
 
 namespace cuvit::gemm {
 
@@ -24,6 +23,9 @@ int launch_tc_bf16(const Plan& plan, cudaStream_t stream) {
 
 namespace {
 
+// Devices whose resident-pair count each pair instance records.
+constexpr int kMaxResidentDevices = 64;
+
 template <int BN>
 int launch_pair_instance(const Plan& plan, cudaStream_t stream) {
     using Shape = PairShape<BN>;
@@ -37,25 +39,29 @@ int launch_pair_instance(const Plan& plan, cudaStream_t stream) {
     attributes[1].val.programmaticStreamSerializationAllowed = 1;
 
     // Shared-memory limit and the number of pairs that can be resident at once (the
-    // persistent grid), both once per process.
-    static std::once_flag once;
-    static cudaError_t setup_error = cudaSuccess;
-    static int resident_pairs = 0;
-    std::call_once(once, [&]() {
-        setup_error = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           Shape::kSmemBytes);
-        if (setup_error != cudaSuccess) {
-            return;
-        }
-        cudaLaunchConfig_t probe{};
-        probe.gridDim = dim3(2, 1, 1);
-        probe.blockDim = dim3(Shape::kThreads, 1, 1);
-        probe.dynamicSmemBytes = Shape::kSmemBytes;
-        probe.attrs = attributes;
-        probe.numAttrs = 1;
-        setup_error = cudaOccupancyMaxActiveClusters(&resident_pairs, kernel, &probe);
-    });
-    CUVIT_TRY_CUDA(setup_error);
+    // persistent grid), both once per device.
+    static int resident[kMaxResidentDevices] = {};
+    int device = 0;
+    CUVIT_TRY_CUDA(cudaGetDevice(&device));
+    if (device < 0 || device >= kMaxResidentDevices) {
+        return host::fail(CUVIT_UNSUPPORTED, "device ordinal out of range");
+    }
+    CUVIT_TRY_CUDA(host::once_per_device(
+        reinterpret_cast<const void*>(kernel), [&](int current) {
+            cudaError_t error = cudaFuncSetAttribute(
+                kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Shape::kSmemBytes);
+            if (error != cudaSuccess) {
+                return error;
+            }
+            cudaLaunchConfig_t probe{};
+            probe.gridDim = dim3(2, 1, 1);
+            probe.blockDim = dim3(Shape::kThreads, 1, 1);
+            probe.dynamicSmemBytes = Shape::kSmemBytes;
+            probe.attrs = attributes;
+            probe.numAttrs = 1;
+            return cudaOccupancyMaxActiveClusters(&resident[current], kernel, &probe);
+        }));
+    const int resident_pairs = resident[device];
     if (resident_pairs < 1) {
         return host::fail(CUVIT_RUNTIME_ERROR,
                           "no CTA pair of the GEMM kernel fits on this device");

@@ -1,10 +1,9 @@
 // Shared body of the per-type launcher translation units: picks the template instantiation
-// for (block_n, b_mn_major), raises its dynamic shared memory limit once, and launches.
+// for (block_n, b_mn_major), raises its dynamic shared memory limit (once per device), and
+// launches.
 #pragma once
 
 #include "gemm.hpp"
-
-#include <mutex>
 
 namespace cuvit::gemm {
 
@@ -12,13 +11,8 @@ template <int ElemBytes, int BN, bool BMn, bool Split>
 int launch_instance(const Plan& plan, cudaStream_t stream) {
     using Shape = TcShape<ElemBytes, BN, Split>;
     auto* kernel = &tc_gemm_kernel<ElemBytes, BN, BMn, Split>;
-    static std::once_flag once;
-    static cudaError_t attribute_error = cudaSuccess;
-    std::call_once(once, [kernel]() {
-        attribute_error = cudaFuncSetAttribute(
-            kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Shape::kSmemBytes);
-    });
-    CUVIT_TRY_CUDA(attribute_error);
+    CUVIT_TRY_CUDA(host::allow_dynamic_smem(reinterpret_cast<const void*>(kernel),
+                                            Shape::kSmemBytes));
     host::pdl_launch(kernel, plan.grid, Shape::kThreads, Shape::kSmemBytes, stream, plan.map_a,
                      plan.map_b, plan.map_c, plan.params);
     return host::after_launch("tc_gemm_kernel");

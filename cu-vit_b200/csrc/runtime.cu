@@ -5,6 +5,7 @@
 #include <algorithm>
 #include <atomic>
 #include <cstring>
+#include <map>
 #include <mutex>
 #include <string>
 #include <vector>
@@ -96,6 +97,33 @@ int current_context(const DeviceContext** context) {
 }
 
 bool is_blackwell(const DeviceContext& context) { return context.major == 10; }
+
+namespace {
+std::mutex g_once_mutex;
+std::map<std::pair<const void*, int>, cudaError_t> g_once_results;
+} // namespace
+
+cudaError_t once_per_device(const void* key, const std::function<cudaError_t(int device)>& setup) {
+    int device = 0;
+    const cudaError_t error = cudaGetDevice(&device);
+    if (error != cudaSuccess) {
+        return error;
+    }
+    const std::lock_guard<std::mutex> lock(g_once_mutex);
+    const auto found = g_once_results.find({key, device});
+    if (found != g_once_results.end()) {
+        return found->second;
+    }
+    const cudaError_t result = setup(device);
+    g_once_results.emplace(std::make_pair(key, device), result);
+    return result;
+}
+
+cudaError_t allow_dynamic_smem(const void* kernel, int bytes) {
+    return once_per_device(kernel, [kernel, bytes](int) {
+        return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    });
+}
 
 int peek_device_status() {
     const DeviceContext* context = nullptr;

@@ -9,6 +9,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <functional>
 #include <string>
 #include <utility>
 
@@ -100,6 +101,15 @@ int peek_device_status();
 
 // True for sm_100 parts, where the tcgen05 kernels can run.
 bool is_blackwell(const DeviceContext& context);
+
+// Runs setup(device) once per (key, current device) and returns its result, then and on every
+// later call for that pair. Kernel attributes (the dynamic shared-memory limit) and occupancy
+// are per device: a process driving several GPUs must set them on each, not once per process.
+cudaError_t once_per_device(const void* key, const std::function<cudaError_t(int device)>& setup);
+
+// Raises kernel's dynamic shared-memory limit to `bytes` on the current device (once per
+// device).
+cudaError_t allow_dynamic_smem(const void* kernel, int bytes);
 
 using TensorMapEncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
                                        const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
