@@ -19,7 +19,9 @@
 namespace cuvit::pre {
 namespace {
 
-constexpr int kThreads = 256;
+constexpr int kStripColumns = 32; // output columns per block (threadIdx.x)
+constexpr int kRowsPerBlock = 8;  // rows a block covers per step (threadIdx.y)
+constexpr int kThreads = kStripColumns * kRowsPerBlock;
 
 struct Params {
     int width;
@@ -31,56 +33,90 @@ struct Params {
     float step;
     float mean[3];
     float stddev[3];
+    // 1 / stddev when every stddev is a power of two (then x / stddev == x * (1 / stddev)
+    // exactly: both are the one rounding of the same real number), else zeros.
+    float inverse_stddev[3];
+    int multiply;
 };
 
-__device__ __forceinline__ float tap(const uint8_t* image, const Params& p, int column, int row,
-                                     int channel) {
-    column = min(max(column, 0), p.width - 1);
-    row = min(max(row, 0), p.height - 1);
-    return static_cast<float>(
-        __ldg(image + (static_cast<long long>(row) * p.width + column) * 3 + channel));
+// Exact conversions that keep the per-pixel work off the special-function (XU) pipe, which
+// the conversions alone would saturate (about 26 XU operations per output pixel). An integer
+// 0 <= v < 2^23 OR-ed into the mantissa of 2^23 is the float 2^23 + v, so subtracting 2^23
+// leaves float(v); adding 1.5 * 2^23 to a float of magnitude below 2^22 rounds it to the
+// nearest integer, held in the low mantissa bits.
+__device__ __forceinline__ float small_int_to_float(uint32_t v) {
+    return __fsub_rn(__uint_as_float(0x4B000000u | v), 8388608.0F);
 }
 
-// The planar output of image blockIdx.y, pixels in grid-stride order.
+// float(int(floor(x))) for |x| < 2^22 (so +0.0 where floor(x) is a zero).
+__device__ __forceinline__ float floor_small(float x) {
+    const float nearest = __fsub_rn(__fadd_rn(x, 12582912.0F), 12582912.0F);
+    return nearest > x ? __fsub_rn(nearest, 1.0F) : nearest;
+}
+
+// The int value of an integral float f, |f| < 2^22.
+__device__ __forceinline__ int integral_to_int(float f) {
+    return __float_as_int(__fadd_rn(f, 12582912.0F)) - 0x4B400000;
+}
+
+// Image blockIdx.z. A block is 32 output columns (threadIdx.x) by 8 rows (threadIdx.y) of a
+// column strip; a thread keeps its column, so the horizontal half of the source map (x, its
+// taps and weights) is computed once, and walks the rows blockIdx.y * 8 + threadIdx.y,
+// stepping gridDim.y * 8.
 __global__ void __launch_bounds__(kThreads)
     preprocess_kernel(const uint8_t* __restrict__ pixels, float* __restrict__ tensor,
                       const Params p) {
     dev::grid_dependency_wait();
     dev::grid_launch_dependents();
-    const int image_index = static_cast<int>(blockIdx.y);
+    const int column = static_cast<int>(blockIdx.x) * kStripColumns + static_cast<int>(threadIdx.x);
+    if (column >= p.size) {
+        return;
+    }
+    const int image_index = static_cast<int>(blockIdx.z);
     const uint8_t* const image = pixels + static_cast<long long>(image_index) * p.image_stride;
-    const long long plane = static_cast<long long>(p.size) * p.size;
+    const int plane = p.size * p.size; // at most 46340^2 < 2^31 (checked on the host)
     float* const out = tensor + static_cast<long long>(image_index) * 3 * plane;
-    for (long long i = static_cast<long long>(blockIdx.x) * kThreads + threadIdx.x; i < plane;
-         i += static_cast<long long>(gridDim.x) * kThreads) {
-        const int row = static_cast<int>(i / p.size);
-        const int column = static_cast<int>(i - static_cast<long long>(row) * p.size);
-        // x = origin_x + (column + 0.5) * step - 0.5, left to right (image.cpp:127-128)
-        const float x = __fsub_rn(
-            __fadd_rn(p.origin_x, __fmul_rn(__fadd_rn(static_cast<float>(column), 0.5F), p.step)),
-            0.5F);
+    const long long row_bytes = static_cast<long long>(p.width) * 3;
+    // x = origin_x + (column + 0.5) * step - 0.5, left to right (image.cpp:127-128); the
+    // taps (image.cpp:39-56): left = int(floor(x)), dx = x - float(left), clamped neighbours.
+    const float x = __fsub_rn(
+        __fadd_rn(p.origin_x,
+                  __fmul_rn(__fadd_rn(small_int_to_float(static_cast<uint32_t>(column)), 0.5F),
+                            p.step)),
+        0.5F);
+    const float left_f = floor_small(x);
+    const int left = integral_to_int(left_f);
+    const float dx = __fsub_rn(x, left_f);
+    const float wx = __fsub_rn(1.0F, dx);
+    const int c0 = 3 * min(max(left, 0), p.width - 1);
+    const int c1 = 3 * min(max(left + 1, 0), p.width - 1);
+    for (int row = static_cast<int>(blockIdx.y) * kRowsPerBlock + static_cast<int>(threadIdx.y);
+         row < p.size; row += static_cast<int>(gridDim.y) * kRowsPerBlock) {
         const float y = __fsub_rn(
-            __fadd_rn(p.origin_y, __fmul_rn(__fadd_rn(static_cast<float>(row), 0.5F), p.step)),
+            __fadd_rn(p.origin_y,
+                      __fmul_rn(__fadd_rn(small_int_to_float(static_cast<uint32_t>(row)), 0.5F),
+                                p.step)),
             0.5F);
-        const float fx = floorf(x);
-        const float fy = floorf(y);
-        const int left = static_cast<int>(fx);
-        const int top = static_cast<int>(fy);
-        const float dx = __fsub_rn(x, static_cast<float>(left));
-        const float dy = __fsub_rn(y, static_cast<float>(top));
-        const float wx = __fsub_rn(1.0F, dx);
+        const float top_f = floor_small(y);
+        const int top = integral_to_int(top_f);
+        const float dy = __fsub_rn(y, top_f);
         const float wy = __fsub_rn(1.0F, dy);
+        const uint8_t* const r0 = image + min(max(top, 0), p.height - 1) * row_bytes;
+        const uint8_t* const r1 = image + min(max(top + 1, 0), p.height - 1) * row_bytes;
+        const int i = row * p.size + column;
 #pragma unroll
         for (int channel = 0; channel < 3; ++channel) {
-            const float top_edge = __fadd_rn(__fmul_rn(tap(image, p, left, top, channel), wx),
-                                             __fmul_rn(tap(image, p, left + 1, top, channel), dx));
-            const float bottom_edge =
-                __fadd_rn(__fmul_rn(tap(image, p, left, top + 1, channel), wx),
-                          __fmul_rn(tap(image, p, left + 1, top + 1, channel), dx));
+            const float tl = small_int_to_float(__ldg(r0 + c0 + channel));
+            const float tr = small_int_to_float(__ldg(r0 + c1 + channel));
+            const float bl = small_int_to_float(__ldg(r1 + c0 + channel));
+            const float br = small_int_to_float(__ldg(r1 + c1 + channel));
+            const float top_edge = __fadd_rn(__fmul_rn(tl, wx), __fmul_rn(tr, dx));
+            const float bottom_edge = __fadd_rn(__fmul_rn(bl, wx), __fmul_rn(br, dx));
             const float sample = __fadd_rn(__fmul_rn(top_edge, wy), __fmul_rn(bottom_edge, dy));
-            const float value = __fdiv_rn(sample, 255.0F);
-            out[channel * plane + i] =
-                __fdiv_rn(__fsub_rn(value, p.mean[channel]), p.stddev[channel]);
+            const float centred = __fsub_rn(__fdiv_rn(sample, 255.0F), p.mean[channel]);
+            out[channel * plane + i] = p.multiply != 0
+                                           ? __fmul_rn(centred, p.inverse_stddev[channel])
+                                           : __fdiv_rn(centred, p.stddev[channel]);
         }
     }
 }
@@ -144,6 +180,13 @@ int cuvit_preprocess(const uint8_t* pixels, int batch, int width, int height,
     if (batch > 65535) {
         return fail(CUVIT_LENGTH_ERROR, "preprocessing launch exceeds the CUDA grid limit");
     }
+    // The device kernel's exact integer/float conversions hold coordinates below 2^22 and its
+    // output plane in 32-bit indices.
+    if (width >= (1 << 22) || height >= (1 << 22) || settings->size > 46340) {
+        return fail(CUVIT_LENGTH_ERROR,
+                    "device preprocessing takes images below 4194304 pixels a side and sizes "
+                    "up to 46340");
+    }
 
     // The source window of the output (image.cpp:103-111), on the host in float as there.
     cuvit::pre::Params p{};
@@ -159,19 +202,35 @@ int cuvit_preprocess(const uint8_t* pixels, int batch, int width, int height,
     p.origin_x = (static_cast<float>(width) - crop) * 0.5F;
     p.origin_y = (static_cast<float>(height) - crop) * 0.5F;
     p.step = crop / static_cast<float>(settings->size);
+    p.multiply = 1;
     for (int c = 0; c < 3; ++c) {
         p.mean[c] = settings->mean[c];
         p.stddev[c] = settings->stddev[c];
+        // A power of two whose reciprocal is a normal float: dividing by it and multiplying by
+        // the reciprocal give the same rounding of the same real number.
+        int exponent = 0;
+        const float mantissa = std::frexp(settings->stddev[c], &exponent);
+        const bool power_of_two = std::fabs(mantissa) == 0.5F && exponent >= -124 &&
+                                  exponent <= 126;
+        p.inverse_stddev[c] = power_of_two ? 1.0F / settings->stddev[c] : 0.0F;
+        p.multiply = p.multiply != 0 && power_of_two ? 1 : 0;
     }
 
     const cuvit::host::DeviceContext* device = nullptr;
     CUVIT_TRY(cuvit::host::current_context(&device));
-    const long long plane = static_cast<long long>(settings->size) * settings->size;
-    long long blocks = (plane + cuvit::pre::kThreads - 1) / cuvit::pre::kThreads;
-    const long long cap = 4LL * device->sm_count * 8 / batch + 1;
-    blocks = blocks < cap ? blocks : cap;
-    const dim3 grid(static_cast<unsigned>(blocks), static_cast<unsigned>(batch));
-    cuvit::host::pdl_launch(cuvit::pre::preprocess_kernel, grid, cuvit::pre::kThreads, 0,
+    // Column strips x row groups x images; enough row groups for about four waves of
+    // resident blocks, each thread then walking size / (8 * groups) rows.
+    const int strips = (settings->size + cuvit::pre::kStripColumns - 1) / cuvit::pre::kStripColumns;
+    const long long wanted_blocks = 4LL * device->sm_count * (2048 / cuvit::pre::kThreads);
+    const long long per_group = static_cast<long long>(strips) * batch;
+    long long groups = (wanted_blocks + per_group - 1) / per_group;
+    const long long max_groups =
+        (settings->size + cuvit::pre::kRowsPerBlock - 1) / cuvit::pre::kRowsPerBlock;
+    groups = groups < 1 ? 1 : (groups > max_groups ? max_groups : groups);
+    const dim3 grid(static_cast<unsigned>(strips), static_cast<unsigned>(groups),
+                    static_cast<unsigned>(batch));
+    const dim3 block(cuvit::pre::kStripColumns, cuvit::pre::kRowsPerBlock);
+    cuvit::host::pdl_launch(cuvit::pre::preprocess_kernel, grid, block, 0,
                             reinterpret_cast<cudaStream_t>(stream), pixels, tensor, p);
     return cuvit::host::after_launch("preprocess_kernel");
 }

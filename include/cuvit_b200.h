@@ -240,7 +240,9 @@ void cuvit_preprocessing_default(cuvit_preprocessing* settings);
  * apart (0 = packed, width * height * 3). tensor: device float [batch, 3, size, size], the
  * layout cuvit_vit_forward reads. Rejects what the reference rejects (empty image, size <= 0,
  * crop fraction outside (0, 1], a zero deviation) with CUVIT_INVALID_ARGUMENT and its
- * message, before any launch. */
+ * message, before any launch; images of 2^22 pixels or more a side, sizes above 46340 and
+ * batches above 65535 with CUVIT_LENGTH_ERROR (limits of the device kernel, not the
+ * reference's). */
 int cuvit_preprocess(const uint8_t* pixels, int batch, int width, int height,
                      int64_t image_stride, const cuvit_preprocessing* settings, float* tensor,
                      cuvit_stream_t stream);

@@ -254,6 +254,11 @@ def test_preprocess_validation_matches_reference():
         kernels.launch_preprocess(FAKE, FAKE, 2, 8, 8, 4, image_stride=8 * 8 * 3 - 1)
     with pytest.raises(InvalidArgument):
         kernels.launch_preprocess(None, FAKE, 1, 8, 8, 4)
+    # The device kernel's own limits (exact float/int conversions below 2^22, 32-bit planes).
+    with pytest.raises(LengthError, match="4194304"):
+        kernels.launch_preprocess(FAKE, FAKE, 1, 1 << 22, 8, 4)
+    with pytest.raises(LengthError, match="46340"):
+        kernels.launch_preprocess(FAKE, FAKE, 1, 8, 8, 46341)
     settings = _lib.PreprocessingC()
     _lib.library().cuvit_preprocessing_default(ctypes.byref(settings))
     assert settings.size == 224 and abs(settings.crop_fraction - 0.9) < 1e-7
