@@ -338,7 +338,10 @@ constexpr int kPipeThreads = 640;
 constexpr int kPipeSoftmaxWarps = 16;
 constexpr int kPipeSlabBytes = 32 * 64; // one warp's 32 context rows x 32 bf16 features
 constexpr int kPipeExchangeBytes = 2 * 2 * 2 * kTileQ * 4; // {extreme, sum} x tile x half x row
-constexpr int kPipeBarriers = 14;
+// buf_full[2], buf_empty[2], s_full[2], p_full[2], o_full[2], o_free[2], drain[2], then the
+// partner exchanges: {extreme, sum} x query tile x lane quarter
+constexpr int kPipeExchangeBarrier = 14;
+constexpr int kPipeBarriers = kPipeExchangeBarrier + 2 * 2 * 4;
 // Key pairs of a 32-key chunk whose exponentials run on the FMA pipe (exp2_poly2), as a bit
 // mask over the chunk's 16 pairs; the others use the special-function unit. The split
 // balances that unit against the issue slots the polynomial takes: with the packed FP32
@@ -411,6 +414,9 @@ __global__ void __launch_bounds__(kPipeThreads, 1)
         }
         dev::mbar_init(bar_drain0, 1);
         dev::mbar_init(bar_drain1, 1);
+        for (int x = 0; x < 2 * 2 * 4; ++x) {
+            dev::mbar_init(bar_base + 8u * (kPipeExchangeBarrier + x), 64); // two warps
+        }
         dev::fence_barrier_init();
     }
     if (warp == 2) {
@@ -528,7 +534,12 @@ __global__ void __launch_bounds__(kPipeThreads, 1)
         float* const x_extreme =
             reinterpret_cast<float*>(smem + exchange_offset) + t * 2 * kTileQ;
         float* const x_sum = x_extreme + 2 * 2 * kTileQ;
-        const uint32_t partner_barrier = 1u + static_cast<uint32_t>(t * 4 + quarter);
+        // The two warps (key halves) of one query tile and lane quarter exchange row extreme
+        // and row sum over mbarriers, whose waits are bounded like every other wait here: a
+        // warp that gave up (another CTA timed out) cannot leave its partner blocked.
+        const uint32_t extreme_bar =
+            bar_base + 8u * static_cast<uint32_t>(kPipeExchangeBarrier + t * 4 + quarter);
+        const uint32_t sum_bar = extreme_bar + 8u * 8u;
         // This warp's 32-column score chunks [c_begin, c_end) and where its P goes.
         const int chunks_all = (p.n_keys + 31) / 32;
         const int c_begin = h == 0 ? 0 : p.split / 32;
@@ -598,7 +609,10 @@ __global__ void __launch_bounds__(kPipeThreads, 1)
                     float extreme = positive ? fmaxf(fmaxf(ext[0], ext[1]), fmaxf(ext[2], ext[3]))
                                              : fminf(fminf(ext[0], ext[1]), fminf(ext[2], ext[3]));
                     x_extreme[h * kTileQ + row] = extreme;
-                    dev::named_barrier_sync(partner_barrier, 64);
+                    dev::mbar_arrive(extreme_bar);
+                    if (!dev::mbar_wait_warp(extreme_bar, parity, p.status)) {
+                        break;
+                    }
                     const float other = x_extreme[(h ^ 1) * kTileQ + row];
                     extreme = positive ? fmaxf(extreme, other) : fminf(extreme, other);
                     const float offset = extreme * p.scale_log2;
@@ -663,7 +677,10 @@ __global__ void __launch_bounds__(kPipeThreads, 1)
                     const float partial = (s01.x + s01.y) + (s23.x + s23.y);
                     x_sum[h * kTileQ + row] = partial;
                     dev::tmem_wait_store();
-                    dev::named_barrier_sync(partner_barrier, 64);
+                    dev::mbar_arrive(sum_bar);
+                    if (!dev::mbar_wait_warp(sum_bar, parity, p.status)) {
+                        break;
+                    }
                     sum = partial + x_sum[(h ^ 1) * kTileQ + row];
                 }
                 dev::tc_fence_before();
