@@ -169,12 +169,6 @@ __device__ __forceinline__ void grid_launch_dependents() {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
-// Synchronises `threads` threads (a multiple of 32) on hardware barrier `id` (1..15; 0 is
-// __syncthreads), ordering their shared-memory accesses.
-__device__ __forceinline__ void named_barrier_sync(uint32_t id, uint32_t threads) {
-    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
-}
-
 // Four floats from / to a 16-byte aligned shared-memory address.
 __device__ __forceinline__ void ld_shared_v4(uint32_t address, float (&v)[4]) {
     asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
