@@ -150,13 +150,25 @@ ReverseSweep::ReverseSweep(bool reverse) : previous_(t_reverse_sweep) {
 
 ReverseSweep::~ReverseSweep() { t_reverse_sweep = previous_; }
 
+thread_local bool t_dependent_launch = false;
+
 bool pdl_enabled() {
-    static const bool enabled = []() {
+    // CUVIT_PDL=1 or 0 decides for every launch; unset, the innermost DependentLaunch does.
+    static const int forced = []() {
         const char* value = std::getenv("CUVIT_PDL");
-        return value != nullptr && std::strcmp(value, "1") == 0;
+        if (value == nullptr) {
+            return -1;
+        }
+        return std::strcmp(value, "1") == 0 ? 1 : (std::strcmp(value, "0") == 0 ? 0 : -1);
     }();
-    return enabled;
+    return forced >= 0 ? forced == 1 : t_dependent_launch;
 }
+
+DependentLaunch::DependentLaunch(bool enable) : previous_(t_dependent_launch) {
+    t_dependent_launch = enable;
+}
+
+DependentLaunch::~DependentLaunch() { t_dependent_launch = previous_; }
 
 int tensor_map_encoder(TensorMapEncodeFn* function) {
     static TensorMapEncodeFn cached = nullptr;

@@ -40,10 +40,24 @@ void clear_error();
 // After a launch: map cudaGetLastError() to a status and count the launch.
 int after_launch(const char* kernel);
 
-// Whether kernels are launched with programmatic stream serialization (dependent launch):
-// only when the environment sets CUVIT_PDL=1. Off by default because on the power-capped
-// B200 the ViT-B/16 BF16 forward measured about 3% slower with it (graph replay, B=256).
+// Whether kernels are launched with programmatic stream serialization (dependent launch), so
+// that a kernel's prologue overlaps the tail of the one before it: inside a DependentLaunch
+// scope that enables it on this thread, or always / never when the environment sets
+// CUVIT_PDL=1 / 0. The model runner enables it for small passes only: ViT-Ti/16 TF32 at
+// batch 32 ran 5% faster with it, while the power-capped ViT-B/16 BF16 pass at batch 256 ran
+// about 3% slower (the overlap raises power draw, and the clock drops).
 bool pdl_enabled();
+
+class DependentLaunch {
+  public:
+    explicit DependentLaunch(bool enable);
+    ~DependentLaunch();
+    DependentLaunch(const DependentLaunch&) = delete;
+    DependentLaunch& operator=(const DependentLaunch&) = delete;
+
+  private:
+    bool previous_;
+};
 
 // Launches a kernel of this library with the programmatic-stream-serialization attribute
 // when enabled (every kernel here waits on griddepcontrol before touching global memory).

@@ -500,6 +500,9 @@ int run_block(cuvit_vit& m, const BlockWeights& w, int layer, int batch, cudaStr
     return CUVIT_OK;
 }
 
+// Passes below this many GEMM FLOPs launch their kernels with programmatic dependent launch.
+constexpr double kDependentLaunchMaxFlops = 2.0e12;
+
 // images: planar FP32 images, or (bf16_images) the same rounded to bfloat16 by the host.
 int run_forward(cuvit_vit& m, const void* images, float* logits, int batch, cudaStream_t stream,
                 Recorder* recorder = nullptr, bool bf16_images = false) {
@@ -514,6 +517,16 @@ int run_forward(cuvit_vit& m, const void* images, float* logits, int batch, cuda
     const double b = batch;
     const cuvit_stream_t s = reinterpret_cast<cuvit_stream_t>(stream);
     bool reverse = false;
+    // Small passes launch each kernel as a dependent of the previous one (its prologue
+    // overlaps the previous tail); large ones do not, since on the power-capped B200 the
+    // overlap costs clock (runtime.hpp, pdl_enabled). The measure is the pass's GEMM work:
+    // ViT-Ti/16 at batch 32 is 0.07 TFLOP, ViT-S/16 at 128 1.2, ViT-B/16 at 256 9.
+    const double per_layer =
+        2.0 * tokens * (double(e) * 3 * e + double(e) * e + 2.0 * double(e) * c.mlp_hidden);
+    const double pass_flops =
+        b * (2.0 * patch_count * double(patch_elements) * e + c.depth * per_layer +
+             2.0 * double(e) * c.classes);
+    const cuvit::host::DependentLaunch overlap(pass_flops < kDependentLaunchMaxFlops);
 
     if (bf16_images) {
         CUVIT_LAUNCH(CUVIT_KIND_PATCHES, -1, 0.0, b * patch_count * patch_elements * (2 + es),
