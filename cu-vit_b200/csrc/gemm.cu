@@ -213,15 +213,20 @@ bool add_batch_dims(const cuvit_gemm_batch& batch, long long stride, long long o
     return true;
 }
 
-// Tile width: the one that wastes least padding, with a preference for wide tiles (fewer
-// re-reads of A, fewer shared-memory and L2 bytes per MMA). For BF16 the preference is
-// stronger: a 128-wide tile needs about 64 FLOP per operand byte, which at the BF16 tensor
-// rate asks more of L2 than it gives (ViT-S/16 QKV, N = 1152, K = 384: 374 us per pass on
-// 256-wide pair tiles, 11% padding, against 448 on 128-wide tiles). N = 384 stays 128 wide
-// (33% padding: its projection measured 350 vs 315 us per pass on 256-wide tiles).
-int choose_block_n(int n, bool split, bool bf16) {
+// Tile width: the one whose tiles finish soonest, counting whole waves of tiles over the SMs
+// (tiles = 128-row blocks x column tiles x batch entries), each wave as long as its tile is
+// wide, with a preference for wide tiles (fewer re-reads of A, fewer shared-memory and L2
+// bytes per MMA). With many waves this is the width that wastes least padding; with few
+// (ViT-Ti/16 at batch 32: M = 6304, 50 row blocks) it avoids a nearly empty last wave. For
+// BF16 the preference is stronger: a 128-wide tile needs about 64 FLOP per operand byte, which
+// at the BF16 tensor rate asks more of L2 than it gives (ViT-S/16 QKV, N = 1152, K = 384:
+// 374 us per pass on 256-wide pair tiles, 11% padding, against 448 on 128-wide tiles).
+// N = 384 stays 128 wide (33% padding: its projection measured 350 vs 315 us per pass on
+// 256-wide tiles). Per-element results do not depend on the width: every tile reduces K in
+// the same order.
+int choose_block_n(long long row_blocks, int n, bool split, bool bf16, int sm_count) {
     const int candidates[] = {256, 128, 64};
-    const double penalty[] = {1.0, bf16 ? 1.2 : 1.1, 1.25};
+    const double penalty[] = {1.0, bf16 ? 1.2 : 1.1, 1.4};
     int best = split ? 128 : 256;
     double best_cost = 1e300;
     for (int i = 0; i < 3; ++i) {
@@ -229,7 +234,9 @@ int choose_block_n(int n, bool split, bool bf16) {
         if (split && bn > 128) {
             continue;
         }
-        const double cost = static_cast<double>((n + bn - 1) / bn) * bn * penalty[i];
+        const long long tiles = row_blocks * ((n + bn - 1) / bn);
+        const long long waves = (tiles + sm_count - 1) / sm_count;
+        const double cost = static_cast<double>(waves) * bn * penalty[i];
         if (cost < best_cost) {
             best_cost = cost;
             best = bn;
@@ -311,7 +318,8 @@ int prepare(const Resolved& r, Plan* plan) {
     const int e = bf16 ? 2 : 4;
     const int block_k = kSwizzleBytes / e;
     const int atom = kSwizzleBytes / e;
-    const int bn = choose_block_n(p.n, split, bf16);
+    const long long row_blocks = (p.m + kBlockM - 1LL) / kBlockM * p.batch.count;
+    const int bn = choose_block_n(row_blocks, p.n, split, bf16, context->sm_count);
     // CTA pairs for BF16 with the weights' K-major layout and 256-wide tiles, once there are
     // at least as many 256-row tiles as SMs (two per pair), so the pairs stay busy. A GELU
     // epilogue keeps the one-CTA kernel: its issue slots, not operand traffic, bound it
