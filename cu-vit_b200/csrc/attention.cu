@@ -30,6 +30,22 @@ constexpr int kHeadDim = 64;
 constexpr int kTileQ = 128;
 constexpr int kMaxTokens = 256;
 constexpr int kThreads = 192; // warp 0 issuer, warp 1 TMEM, warps 2..5 softmax
+// The FP32/TF32 instance: 16 softmax warps, the four of each TMEM lane quarter splitting the
+// key chunks of its rows (P is stored in place there, so no column remapping is needed).
+constexpr int kSplitSoftmaxWarps = 16;
+constexpr int kSplitThreads = 64 + 32 * kSplitSoftmaxWarps;
+// Row extreme and row sum of the four parts of each row, then the exchange barriers.
+constexpr int kSplitExchangeBytes = 2 * 4 * 128 * 4;
+
+template <int ElemBytes>
+__host__ __device__ constexpr int softmax_warps() {
+    return ElemBytes == 4 ? kSplitSoftmaxWarps : 4;
+}
+
+template <int ElemBytes>
+__host__ __device__ constexpr int kernel_threads() {
+    return ElemBytes == 4 ? kSplitThreads : kThreads;
+}
 
 struct Params {
     int tokens;
@@ -57,7 +73,7 @@ struct Layout {
 };
 
 template <int ElemBytes>
-__global__ void __launch_bounds__(kThreads)
+__global__ void __launch_bounds__(kernel_threads<ElemBytes>())
     attention_kernel(const __grid_constant__ CUtensorMap map_q,
                      const __grid_constant__ CUtensorMap map_kv,
                      const __grid_constant__ CUtensorMap map_v, const Params p) {
@@ -87,7 +103,10 @@ __global__ void __launch_bounds__(kThreads)
     const uint32_t bar_o = bar_base + 24;
     const uint32_t bar_free = bar_base + 32;
     const uint32_t bar_drain = bar_base + 40;
-    uint32_t* const tmem_slot = reinterpret_cast<uint32_t*>(smem + (bar_base - base) + 48);
+    const uint32_t bar_exchange = bar_base + 48; // {extreme, sum} x lane quarter (split path)
+    uint32_t* const tmem_slot = reinterpret_cast<uint32_t*>(smem + (bar_base - base) + 112);
+    float* const exchange = reinterpret_cast<float*>(smem + (bar_base - base) + 128);
+    constexpr uint32_t kSoftmaxThreads = 32u * softmax_warps<ElemBytes>();
 
     const int warp = threadIdx.x / 32;
     const int lane = threadIdx.x % 32;
@@ -99,10 +118,13 @@ __global__ void __launch_bounds__(kThreads)
     if (threadIdx.x == 0) {
         dev::mbar_init(bar_load, 1);
         dev::mbar_init(bar_s, 1);
-        dev::mbar_init(bar_p, 128);
+        dev::mbar_init(bar_p, kSoftmaxThreads);
         dev::mbar_init(bar_o, 1);
-        dev::mbar_init(bar_free, 128);
+        dev::mbar_init(bar_free, kSoftmaxThreads);
         dev::mbar_init(bar_drain, 1);
+        for (int x = 0; x < 8; ++x) {
+            dev::mbar_init(bar_exchange + 8u * x, 4 * 32); // the four warps of a quarter
+        }
         dev::fence_barrier_init();
     }
     if (warp == 1) {
@@ -183,6 +205,117 @@ __global__ void __launch_bounds__(kThreads)
             // Wait until every MMA issued so far has finished before the CTA tears down.
             dev::tc_commit(bar_drain);
             dev::mbar_drain_wait(bar_drain, 0);
+        }
+    } else if (ElemBytes == 4 && warp >= 2) {
+        // ---------------- softmax and output, split four ways per row ----------------
+        // Warp w (2..17) has TMEM lane quarter w & 3 and part (w - 2) >> 2 of the key chunks
+        // (32 columns each; parts take chunks / 4, the first chunks % 4 parts one more).
+        const int part = (warp - 2) >> 2;
+        const int quarter = warp & 3;
+        const int row = quarter * 32 + lane;
+        const uint32_t lane_field = static_cast<uint32_t>(quarter * 32) << 16;
+        const int chunks = (p.n_keys + 31) / 32;
+        const int c_begin = part * (chunks >> 2) + (part < (chunks & 3) ? part : (chunks & 3));
+        const int c_end =
+            (part + 1) * (chunks >> 2) + (part + 1 < (chunks & 3) ? part + 1 : (chunks & 3));
+        float* const x_extreme = exchange;        // [part][row]
+        float* const x_sum = exchange + 4 * kTileQ; // [part][row]
+        const uint32_t extreme_bar = bar_exchange + 8u * static_cast<uint32_t>(quarter);
+        const uint32_t sum_bar = extreme_bar + 32u;
+        for (int t = 0; t < p.q_tiles; ++t) {
+            const uint32_t parity = static_cast<uint32_t>(t & 1);
+            if (!dev::mbar_wait_warp(bar_s, parity, p.status)) {
+                break;
+            }
+            dev::tc_fence_after();
+            float maximum = -INFINITY;
+            for (int c = c_begin; c < c_end; ++c) {
+                uint32_t s[32];
+                dev::tmem_load_32(tmem + lane_field + c * 32, s);
+                dev::tmem_wait_load();
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    if (c * 32 + j < p.tokens) {
+                        maximum = fmaxf(maximum, __uint_as_float(s[j]) * p.scale);
+                    }
+                }
+            }
+            // The maximum is exact in any order; the four parts in a fixed order for the sum.
+            x_extreme[part * kTileQ + row] = maximum;
+            dev::mbar_arrive(extreme_bar);
+            if (!dev::mbar_wait_warp(extreme_bar, parity, p.status)) {
+                break;
+            }
+            maximum = fmaxf(fmaxf(x_extreme[row], x_extreme[kTileQ + row]),
+                            fmaxf(x_extreme[2 * kTileQ + row], x_extreme[3 * kTileQ + row]));
+            const float offset = maximum * 1.4426950408889634F;
+            float sum = 0.0F;
+            for (int c = c_begin; c < c_end; ++c) {
+                uint32_t s[32];
+                dev::tmem_load_32(tmem + lane_field + c * 32, s);
+                dev::tmem_wait_load();
+                // P enters the tensor core as TF32: round it here (the MMA would truncate)
+                // and normalise by the sum of exactly these values.
+                uint32_t lo[16];
+                uint32_t hi[16];
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    const float a =
+                        c * 32 + j < p.tokens
+                            ? dev::round_to_tf32(
+                                  exp2f(__uint_as_float(s[j]) * p.scale_log2 - offset))
+                            : 0.0F;
+                    const float b =
+                        c * 32 + 16 + j < p.tokens
+                            ? dev::round_to_tf32(
+                                  exp2f(__uint_as_float(s[16 + j]) * p.scale_log2 - offset))
+                            : 0.0F;
+                    lo[j] = __float_as_uint(a);
+                    hi[j] = __float_as_uint(b);
+                    sum += a + b;
+                }
+                dev::tmem_store_16(tmem + lane_field + c * 32, lo);
+                dev::tmem_store_16(tmem + lane_field + c * 32 + 16, hi);
+            }
+            x_sum[part * kTileQ + row] = sum;
+            dev::tmem_wait_store();
+            dev::tc_fence_before();
+            dev::mbar_arrive(bar_p);
+            dev::mbar_arrive(sum_bar);
+            if (!dev::mbar_wait_warp(sum_bar, parity, p.status)) {
+                break;
+            }
+            sum = (x_sum[row] + x_sum[kTileQ + row]) +
+                  (x_sum[2 * kTileQ + row] + x_sum[3 * kTileQ + row]);
+            if (!dev::mbar_wait_warp(bar_o, parity, p.status)) {
+                break;
+            }
+            dev::tc_fence_after();
+            uint32_t o[16];
+            dev::tmem_load_16(tmem + lane_field + L::kOColumn + 16u * static_cast<uint32_t>(part),
+                              o);
+            dev::tmem_wait_load();
+            const float inverse = 1.0F / sum;
+            const int query = t * kTileQ + row;
+            if (query < p.tokens) {
+                float* const out = static_cast<float*>(p.context) +
+                                   (static_cast<long long>(image) * p.tokens + query) * p.heads *
+                                       kHeadDim +
+                                   head * kHeadDim + 16 * part;
+                float4* const out4 = reinterpret_cast<float4*>(out);
+                const bool round = p.round_output != 0;
+                const auto finish = [inverse, round](uint32_t raw) {
+                    const float value = __uint_as_float(raw) * inverse;
+                    return round ? dev::round_to_tf32(value) : value;
+                };
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    out4[q] = make_float4(finish(o[4 * q]), finish(o[4 * q + 1]),
+                                          finish(o[4 * q + 2]), finish(o[4 * q + 3]));
+                }
+            }
+            dev::tc_fence_before();
+            dev::mbar_arrive(bar_free);
         }
     } else if (warp >= 2) {
         // ---------------- softmax and output ----------------
@@ -902,14 +1035,15 @@ int launch_typed(const void* qkv, void* context, int batch, int tokens, int head
     params.reverse = host::reverse_sweep() ? 1 : 0;
     params.status = device.status;
 
-    int smem = 1024 + q_tiles * L::kQTileBytes + 2 * L::kDAtoms * n_keys * 128 + 64;
+    int smem = 1024 + q_tiles * L::kQTileBytes + 2 * L::kDAtoms * n_keys * 128 + 128 +
+               kSplitExchangeBytes;
     if (smem < L::kMinSmem) {
         smem = L::kMinSmem;
     }
     auto* kernel = &attention_kernel<ElemBytes>;
     CUVIT_TRY_CUDA(host::allow_dynamic_smem(reinterpret_cast<const void*>(kernel), 227 * 1024));
-    host::pdl_launch(kernel, batch * heads, kThreads, smem, stream, map_q, map_kv, map_v,
-                     params);
+    host::pdl_launch(kernel, batch * heads, kernel_threads<ElemBytes>(), smem, stream, map_q,
+                     map_kv, map_v, params);
     return host::after_launch("attention_kernel");
 }
 
