@@ -36,6 +36,10 @@ constexpr int kSplitSoftmaxWarps = 16;
 constexpr int kSplitThreads = 64 + 32 * kSplitSoftmaxWarps;
 // Row extreme and row sum of the four parts of each row, then the exchange barriers.
 constexpr int kSplitExchangeBytes = 2 * 4 * 128 * 4;
+// TMEM columns when both query tiles' scores are held at once (FP32 path, at most 224 keys):
+// tile 1's scores at 224 and O at 448, after the 224 columns of each tile.
+constexpr uint32_t kSecondScores = 224;
+constexpr uint32_t kBothTilesO = 448;
 
 template <int ElemBytes>
 __host__ __device__ constexpr int softmax_warps() {
@@ -104,8 +108,11 @@ __global__ void __launch_bounds__(kernel_threads<ElemBytes>())
     const uint32_t bar_free = bar_base + 32;
     const uint32_t bar_drain = bar_base + 40;
     const uint32_t bar_exchange = bar_base + 48; // {extreme, sum} x lane quarter (split path)
-    uint32_t* const tmem_slot = reinterpret_cast<uint32_t*>(smem + (bar_base - base) + 112);
-    float* const exchange = reinterpret_cast<float*>(smem + (bar_base - base) + 128);
+    // Split path with both query tiles' scores in TMEM at once: tile 1's scores and P.
+    const uint32_t bar_s1 = bar_base + 112;
+    const uint32_t bar_p1 = bar_base + 120;
+    uint32_t* const tmem_slot = reinterpret_cast<uint32_t*>(smem + (bar_base - base) + 128);
+    float* const exchange = reinterpret_cast<float*>(smem + (bar_base - base) + 256);
     constexpr uint32_t kSoftmaxThreads = 32u * softmax_warps<ElemBytes>();
 
     const int warp = threadIdx.x / 32;
@@ -114,6 +121,9 @@ __global__ void __launch_bounds__(kernel_threads<ElemBytes>())
                               : static_cast<int>(blockIdx.x);
     const int image = job / p.heads;
     const int head = job - image * p.heads;
+    // FP32/TF32 with two query tiles and at most 224 keys: both tiles' scores fit TMEM at once.
+    const bool both_tiles = ElemBytes == 4 && p.q_tiles == 2 && p.n_keys <= kSecondScores;
+    const uint32_t o_column = both_tiles ? kBothTilesO : static_cast<uint32_t>(L::kOColumn);
 
     if (threadIdx.x == 0) {
         dev::mbar_init(bar_load, 1);
@@ -125,6 +135,8 @@ __global__ void __launch_bounds__(kernel_threads<ElemBytes>())
         for (int x = 0; x < 8; ++x) {
             dev::mbar_init(bar_exchange + 8u * x, 4 * 32); // the four warps of a quarter
         }
+        dev::mbar_init(bar_s1, 1);
+        dev::mbar_init(bar_p1, kSoftmaxThreads);
         dev::fence_barrier_init();
     }
     if (warp == 1) {
@@ -166,13 +178,7 @@ __global__ void __launch_bounds__(kernel_threads<ElemBytes>())
         const uint32_t idesc_s = dev::make_idesc(kFormat, kTileQ, p.n_keys, false, false);
         constexpr uint32_t kIdescO = dev::make_idesc(kFormat, kTileQ, kHeadDim, false, true);
         constexpr int kStepsPerAtom = L::kAtomElems / L::kMmaK;
-        for (int t = 0; t < p.q_tiles && ok; ++t) {
-            if (t > 0 && !dev::mbar_wait(bar_free, (t - 1) & 1, p.status)) {
-                ok = false;
-                break;
-            }
-            dev::tc_fence_after();
-            // S = Q_t . K^T
+        const auto issue_scores = [&](int t, uint32_t column) {
 #pragma unroll
             for (int kk = 0; kk < kHeadDim / L::kMmaK; ++kk) {
                 const int atom = kk / kStepsPerAtom;
@@ -181,24 +187,57 @@ __global__ void __launch_bounds__(kernel_threads<ElemBytes>())
                     q_smem + t * L::kQTileBytes + atom * kTileQ * 128 + offset, 16, 1024);
                 const uint64_t b_desc =
                     dev::smem_desc_sw128(k_smem + atom * kv_region + offset, 16, 1024);
-                dev::mma_ss<kKind>(tmem, a_desc, b_desc, idesc_s, kk > 0 ? 1u : 0u);
+                dev::mma_ss<kKind>(tmem + column, a_desc, b_desc, idesc_s, kk > 0 ? 1u : 0u);
             }
+        };
+        const auto issue_context = [&](uint32_t column) {
+            // O = P . V, P read from TMEM columns [column, column + n_keys * ElemBytes / 4)
+            const int steps = p.n_keys / L::kMmaK;
+            for (int kk = 0; kk < steps; ++kk) {
+                const uint32_t a_tmem = tmem + column + static_cast<uint32_t>(kk * 8);
+                const uint64_t b_desc =
+                    dev::smem_desc(v_smem + kk * L::kMmaK * 128, static_cast<uint32_t>(kv_region),
+                                   kVAtomBytes, kVLayout);
+                dev::mma_ts<kKind>(tmem + o_column, a_tmem, b_desc, kIdescO,
+                                   kk > 0 ? 1u : 0u);
+            }
+        };
+        if (ok && both_tiles) {
+            // Both tiles' scores at once (tile 1's at column kSecondScores); P.V of tile 0
+            // runs while the softmax warps work on tile 1, P.V of tile 1 once O(0) is read.
+            dev::tc_fence_after();
+            issue_scores(0, 0u);
+            dev::tc_commit(bar_s);
+            issue_scores(1, kSecondScores);
+            dev::tc_commit(bar_s1);
+            ok = dev::mbar_wait(bar_p, 0, p.status);
+            if (ok) {
+                dev::tc_fence_after();
+                issue_context(0u);
+                dev::tc_commit(bar_o);
+                ok = dev::mbar_wait(bar_free, 0, p.status) && dev::mbar_wait(bar_p1, 0, p.status);
+            }
+            if (ok) {
+                dev::tc_fence_after();
+                issue_context(kSecondScores);
+                dev::tc_commit(bar_o);
+            }
+        }
+        for (int t = 0; t < p.q_tiles && ok && !both_tiles; ++t) {
+            // One tile at a time: S(t) reuses the columns of P(t - 1) once O(t - 1) is read.
+            if (t > 0 && !dev::mbar_wait(bar_free, (t - 1) & 1, p.status)) {
+                ok = false;
+                break;
+            }
+            dev::tc_fence_after();
+            issue_scores(t, 0u);
             dev::tc_commit(bar_s);
             if (!dev::mbar_wait(bar_p, t & 1, p.status)) {
                 ok = false;
                 break;
             }
             dev::tc_fence_after();
-            // O = P . V, P read from TMEM columns [0, n_keys * ElemBytes / 4)
-            const int steps = p.n_keys / L::kMmaK;
-            for (int kk = 0; kk < steps; ++kk) {
-                const uint32_t a_tmem = tmem + static_cast<uint32_t>(kk * 8);
-                const uint64_t b_desc =
-                    dev::smem_desc(v_smem + kk * L::kMmaK * 128, static_cast<uint32_t>(kv_region),
-                                   kVAtomBytes, kVLayout);
-                dev::mma_ts<kKind>(tmem + L::kOColumn, a_tmem, b_desc, kIdescO,
-                                   kk > 0 ? 1u : 0u);
-            }
+            issue_context(0u);
             dev::tc_commit(bar_o);
         }
         if (!ok) {
@@ -222,16 +261,20 @@ __global__ void __launch_bounds__(kernel_threads<ElemBytes>())
         float* const x_sum = exchange + 4 * kTileQ; // [part][row]
         const uint32_t extreme_bar = bar_exchange + 8u * static_cast<uint32_t>(quarter);
         const uint32_t sum_bar = extreme_bar + 32u;
-        for (int t = 0; t < p.q_tiles; ++t) {
+        // Softmax of query tile t, whose scores start at TMEM column `column`: P (TF32 values)
+        // in place, the hand-off on `p_bar`, the row sum into `sum`.
+        const auto softmax_tile = [&](int t, uint32_t column, uint32_t s_bar, uint32_t s_parity,
+                                      uint32_t p_bar, float& sum) -> bool {
             const uint32_t parity = static_cast<uint32_t>(t & 1);
-            if (!dev::mbar_wait_warp(bar_s, parity, p.status)) {
-                break;
+            if (!dev::mbar_wait_warp(s_bar, s_parity, p.status)) {
+                return false;
             }
             dev::tc_fence_after();
+            const uint32_t scores = tmem + lane_field + column;
             float maximum = -INFINITY;
             for (int c = c_begin; c < c_end; ++c) {
                 uint32_t s[32];
-                dev::tmem_load_32(tmem + lane_field + c * 32, s);
+                dev::tmem_load_32(scores + c * 32, s);
                 dev::tmem_wait_load();
 #pragma unroll
                 for (int j = 0; j < 32; ++j) {
@@ -244,15 +287,15 @@ __global__ void __launch_bounds__(kernel_threads<ElemBytes>())
             x_extreme[part * kTileQ + row] = maximum;
             dev::mbar_arrive(extreme_bar);
             if (!dev::mbar_wait_warp(extreme_bar, parity, p.status)) {
-                break;
+                return false;
             }
             maximum = fmaxf(fmaxf(x_extreme[row], x_extreme[kTileQ + row]),
                             fmaxf(x_extreme[2 * kTileQ + row], x_extreme[3 * kTileQ + row]));
             const float offset = maximum * 1.4426950408889634F;
-            float sum = 0.0F;
+            float partial = 0.0F;
             for (int c = c_begin; c < c_end; ++c) {
                 uint32_t s[32];
-                dev::tmem_load_32(tmem + lane_field + c * 32, s);
+                dev::tmem_load_32(scores + c * 32, s);
                 dev::tmem_wait_load();
                 // P enters the tensor core as TF32: round it here (the MMA would truncate)
                 // and normalise by the sum of exactly these values.
@@ -272,28 +315,32 @@ __global__ void __launch_bounds__(kernel_threads<ElemBytes>())
                             : 0.0F;
                     lo[j] = __float_as_uint(a);
                     hi[j] = __float_as_uint(b);
-                    sum += a + b;
+                    partial += a + b;
                 }
-                dev::tmem_store_16(tmem + lane_field + c * 32, lo);
-                dev::tmem_store_16(tmem + lane_field + c * 32 + 16, hi);
+                dev::tmem_store_16(scores + c * 32, lo);
+                dev::tmem_store_16(scores + c * 32 + 16, hi);
             }
-            x_sum[part * kTileQ + row] = sum;
+            x_sum[part * kTileQ + row] = partial;
             dev::tmem_wait_store();
             dev::tc_fence_before();
-            dev::mbar_arrive(bar_p);
+            dev::mbar_arrive(p_bar);
             dev::mbar_arrive(sum_bar);
             if (!dev::mbar_wait_warp(sum_bar, parity, p.status)) {
-                break;
+                return false;
             }
             sum = (x_sum[row] + x_sum[kTileQ + row]) +
                   (x_sum[2 * kTileQ + row] + x_sum[3 * kTileQ + row]);
-            if (!dev::mbar_wait_warp(bar_o, parity, p.status)) {
-                break;
+            return true;
+        };
+        // O of query tile t (this warp's 16 columns), scaled by 1 / rowsum and stored; then O
+        // is free for the next P.V.
+        const auto readout_tile = [&](int t, float sum) -> bool {
+            if (!dev::mbar_wait_warp(bar_o, static_cast<uint32_t>(t & 1), p.status)) {
+                return false;
             }
             dev::tc_fence_after();
             uint32_t o[16];
-            dev::tmem_load_16(tmem + lane_field + L::kOColumn + 16u * static_cast<uint32_t>(part),
-                              o);
+            dev::tmem_load_16(tmem + lane_field + o_column + 16u * static_cast<uint32_t>(part), o);
             dev::tmem_wait_load();
             const float inverse = 1.0F / sum;
             const int query = t * kTileQ + row;
@@ -316,6 +363,24 @@ __global__ void __launch_bounds__(kernel_threads<ElemBytes>())
             }
             dev::tc_fence_before();
             dev::mbar_arrive(bar_free);
+            return true;
+        };
+        if (both_tiles) {
+            // Both softmaxes first (tile 0's P.V runs during tile 1's), then both read-outs.
+            float sums[2] = {1.0F, 1.0F};
+            if (softmax_tile(0, 0u, bar_s, 0u, bar_p, sums[0]) &&
+                softmax_tile(1, kSecondScores, bar_s1, 0u, bar_p1, sums[1]) &&
+                readout_tile(0, sums[0])) {
+                readout_tile(1, sums[1]);
+            }
+        } else {
+            for (int t = 0; t < p.q_tiles; ++t) {
+                float sum = 1.0F;
+                if (!softmax_tile(t, 0u, bar_s, static_cast<uint32_t>(t & 1), bar_p, sum) ||
+                    !readout_tile(t, sum)) {
+                    break;
+                }
+            }
         }
     } else if (warp >= 2) {
         // ---------------- softmax and output ----------------
@@ -1035,7 +1100,8 @@ int launch_typed(const void* qkv, void* context, int batch, int tokens, int head
     params.reverse = host::reverse_sweep() ? 1 : 0;
     params.status = device.status;
 
-    int smem = 1024 + q_tiles * L::kQTileBytes + 2 * L::kDAtoms * n_keys * 128 + 128 +
+    // Operand tiles, then barriers and the TMEM slot (256 bytes), then the row exchange.
+    int smem = 1024 + q_tiles * L::kQTileBytes + 2 * L::kDAtoms * n_keys * 128 + 256 +
                kSplitExchangeBytes;
     if (smem < L::kMinSmem) {
         smem = L::kMinSmem;
