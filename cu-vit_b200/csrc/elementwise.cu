@@ -84,7 +84,20 @@ bool valid_storage(int dtype) {
 // row's first element plus that element, which keeps a large common offset from swamping
 // the spread (the reference's origin shift, src/kernels/normalization.cu:59-70); the
 // variance is the biased mean of squared deviations from that mean.
-template <typename Out>
+// Sum over the kLanes lanes of an aligned group of a warp (every lane of the warp takes part).
+template <int kLanes>
+__device__ __forceinline__ float group_sum(float value) {
+#pragma unroll
+    for (int offset = kLanes / 2; offset > 0; offset /= 2) {
+        value += __shfl_xor_sync(0xFFFFFFFFu, value, offset);
+    }
+    return value;
+}
+
+// kLanes lanes per row (32 / kLanes rows per warp), so short rows still give each lane several
+// vectors in flight: 32 for rows of more than 512 floats, 16 above 256, else 8. With 32 the
+// reduction order is the whole-warp one.
+template <typename Out, int kLanes>
 __global__ void __launch_bounds__(kThreads)
     layer_norm_warp_kernel(const float* __restrict__ input, long long in_stride,
                            const float* __restrict__ gamma, const float* __restrict__ beta,
@@ -93,44 +106,46 @@ __global__ void __launch_bounds__(kThreads)
     dev::timeline_enter();
     dev::grid_dependency_wait();
     dev::grid_launch_dependents();
-    const int slot = blockIdx.x * kRowsPerBlock + threadIdx.x / kWarp;
-    const int lane = threadIdx.x % kWarp;
-    if (slot >= rows) {
-        return;
-    }
-    const int row = reverse ? rows - 1 - slot : slot;
+    constexpr int kRowsPerWarp = kWarp / kLanes;
+    const int slot = (blockIdx.x * kRowsPerBlock + threadIdx.x / kWarp) * kRowsPerWarp +
+                     (threadIdx.x % kWarp) / kLanes;
+    const int lane = threadIdx.x % kLanes;
+    // A group past the last row stays for the shuffles of the others in its warp.
+    const bool valid = slot < rows;
+    const int row = valid ? (reverse ? rows - 1 - slot : slot) : 0;
     const float4* const in4 = reinterpret_cast<const float4*>(input + row * in_stride);
     const int vectors = columns / 4;
     float4 x[kMaxVec];
-    const float origin = __ldg(input + row * in_stride);
+    const float origin = valid ? __ldg(input + row * in_stride) : 0.0F;
     float sum = 0.0F;
 #pragma unroll
     for (int i = 0; i < kMaxVec; ++i) {
-        const int v = lane + i * kWarp;
-        if (v < vectors) {
+        const int v = lane + i * kLanes;
+        if (valid && v < vectors) {
             x[i] = __ldg(in4 + v);
             sum += (x[i].x - origin) + (x[i].y - origin) + (x[i].z - origin) + (x[i].w - origin);
         }
     }
-    const float mean = origin + warp_sum(sum) / static_cast<float>(columns);
+    const float mean = origin + group_sum<kLanes>(sum) / static_cast<float>(columns);
     float squares = 0.0F;
 #pragma unroll
     for (int i = 0; i < kMaxVec; ++i) {
-        const int v = lane + i * kWarp;
-        if (v < vectors) {
+        const int v = lane + i * kLanes;
+        if (valid && v < vectors) {
             const float a = x[i].x - mean, b = x[i].y - mean, c = x[i].z - mean,
                         d = x[i].w - mean;
             squares += a * a + b * b + c * c + d * d;
         }
     }
-    const float inverse = rsqrtf(warp_sum(squares) / static_cast<float>(columns) + epsilon);
+    const float inverse =
+        rsqrtf(group_sum<kLanes>(squares) / static_cast<float>(columns) + epsilon);
     const float4* const g4 = reinterpret_cast<const float4*>(gamma);
     const float4* const b4 = reinterpret_cast<const float4*>(beta);
     Out* const out = output + row * out_stride;
 #pragma unroll
     for (int i = 0; i < kMaxVec; ++i) {
-        const int v = lane + i * kWarp;
-        if (v < vectors) {
+        const int v = lane + i * kLanes;
+        if (valid && v < vectors) {
             const float4 g = __ldg(g4 + v);
             const float4 b = __ldg(b4 + v);
             float4 y;
@@ -641,11 +656,16 @@ int layer_norm_impl(const float* input, long long in_stride, const float* gamma,
     const auto run = [&](auto* out) {
         using Out = std::remove_pointer_t<decltype(out)>;
         if (fast) {
+            const int vectors = columns / 4;
+            const int lanes = vectors > 16 * kMaxVec ? 32 : (vectors > 8 * kMaxVec ? 16 : 8);
+            const int rows_per_block = kRowsPerBlock * (kWarp / lanes);
             const unsigned blocks =
-                static_cast<unsigned>((rows + kRowsPerBlock - 1) / kRowsPerBlock);
-            host::pdl_launch(layer_norm_warp_kernel<Out>, blocks, kThreads, 0, stream, input,
-                             in_stride, gamma, beta, out, out_stride, rows, columns, epsilon,
-                             reverse);
+                static_cast<unsigned>((rows + rows_per_block - 1) / rows_per_block);
+            auto* kernel = lanes == 32   ? &layer_norm_warp_kernel<Out, 32>
+                           : lanes == 16 ? &layer_norm_warp_kernel<Out, 16>
+                                         : &layer_norm_warp_kernel<Out, 8>;
+            host::pdl_launch(kernel, blocks, kThreads, 0, stream, input, in_stride, gamma, beta,
+                             out, out_stride, rows, columns, epsilon, reverse);
         } else {
             host::pdl_launch(layer_norm_block_kernel<Out>, rows, kThreads, 0, stream, input,
                              in_stride, gamma, beta, out, out_stride, columns, epsilon,
